@@ -1,0 +1,148 @@
+"""Generate the golden vectors in this directory by running the REFERENCE.
+
+Run once in a container that has the reference checkout (it reads
+echo/stau_opus_operator.py, echo/triton_wta.py and
+echo/patch_whisper_sparse_grad.py from it); the resulting .npz files are
+committed, so tests never need the reference at run time.
+
+    python tests/golden/make_golden.py [/path/to/reference]
+
+Every case is seeded; attention inputs and the reference's outputs are
+stored in fp32, WTA inputs/outputs as raw bf16 bit patterns (uint16) and
+masks as little-endian packed bits.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.nn.functional as Fnn
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _ref_path(argv):
+    if len(argv) > 1:
+        return argv[1]
+    return os.environ.get("TAU_DXB_REFERENCE", "/root/reference")
+
+
+def attn_cases():
+    # (name, sigma, B, H, Lq, Lk, D, scale, mask kind, log_tau spec, seed)
+    return [
+        ("attn_softplus_l65", "softplus", 1, 2, 65, 65, 64, None, None, "normal", 11),
+        ("attn_softplus_l200_s1", "softplus", 1, 2, 200, 200, 64, 1.0, None, "normal", 12),
+        ("attn_sigmoid_causal_l70", "sigmoid", 2, 2, 70, 70, 64, 1.0, "causal", "normal", 13),
+        ("attn_exp_cross_33x100", "exp", 1, 3, 33, 100, 64, 0.125, None, "normal", 14),
+        ("attn_exp_tau1_softmax", "exp", 1, 2, 40, 90, 64, None, None, "tau1", 15),
+        ("attn_softplus_alpha_l17", "softplus", 2, 2, 17, 17, 64, None, None, "alpha", 16),
+        ("attn_sigmoid_l1", "sigmoid", 1, 2, 1, 1, 64, None, None, "normal", 17),
+    ]
+
+
+def make_attn(ref):
+    from stau_opus_operator import STauOpusAttentionFunction as E
+    for (name, sg, B, H, Lq, Lk, D, scale, mk, lt_spec, seed) in attn_cases():
+        g = torch.Generator().manual_seed(seed)
+        Q = torch.randn(B, H, Lq, D, generator=g)
+        K = torch.randn(B, H, Lk, D, generator=g)
+        V = torch.randn(B, H, Lk, D, generator=g)
+        dO = torch.randn(B, H, Lq, D, generator=g)
+        log_tau = torch.randn(H, generator=g) * 0.5
+        log_alpha = torch.zeros(H)
+        if lt_spec == "tau1":
+            log_tau = torch.full((H,), -30.0)
+        if lt_spec == "alpha":
+            log_alpha = torch.randn(H, generator=g) * 0.3
+        mask = None
+        if mk == "causal":
+            mask = torch.full((Lq, Lk), torch.finfo(torch.float32).min).triu(1)[None, None]
+        q, k, v = (t.clone().requires_grad_() for t in (Q, K, V))
+        lt = log_tau.clone().requires_grad_()
+        la = log_alpha.clone().requires_grad_()
+        out, _ = E.apply(q, k, v, lt, la, sg, mask, scale)
+        out.backward(dO)
+        rec = dict(Q=Q.numpy(), K=K.numpy(), V=V.numpy(), dO=dO.numpy(),
+                   log_tau=log_tau.numpy(), log_alpha=log_alpha.numpy(),
+                   out=out.detach().numpy(), dQ=q.grad.numpy(), dK=k.grad.numpy(),
+                   dV=v.grad.numpy(), dlog_tau=lt.grad.numpy(), dlog_alpha=la.grad.numpy(),
+                   sigma=np.array(sg), scale=np.array(np.nan if scale is None else scale,
+                                                       dtype=np.float64))
+        if mask is not None:
+            rec["mask"] = mask.numpy()
+        if lt_spec == "tau1":
+            s = torch.matmul(Q, K.transpose(-1, -2)) * (D ** -0.5 if scale is None else scale)
+            rec["softmax_out"] = torch.matmul(torch.softmax(s, -1), V).numpy()
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
+        print("wrote", name)
+
+
+def make_wta(ref):
+    import triton_wta as T
+    import patch_whisper_sparse_grad as S
+    g = torch.Generator().manual_seed(21)
+    R, D = 48, 3072
+    x = Fnn.gelu(torch.randn(R, D, generator=g)).to(torch.bfloat16)
+    dy = torch.randn(R, D, generator=g).to(torch.bfloat16)
+    bits = x.view(torch.int16).numpy().view(np.uint16)
+    dybits = dy.view(torch.int16).numpy().view(np.uint16)
+    rec = dict(x_bits=bits, dy_bits=dybits)
+    ks = [1, 154, 306, 307, 768, 1536, 3072]
+    rec["ks"] = np.array(ks)
+    for k in ks:
+        # threshold semantics: SparseGradWTA_Function (same rule as the GPU Triton path)
+        xx = x.clone().requires_grad_()
+        out = S.SparseGradWTA_Function.apply(xx, k)
+        out.backward(dy)
+        # the saved mask itself (the backward multiplies dy by it)
+        thr = x.kthvalue(D - k + 1, dim=-1, keepdim=True).values
+        thr_mask = (x >= thr)
+        rec[f"thr_mask_k{k}"] = np.packbits(thr_mask.numpy(), axis=-1, bitorder="little")
+        if k == 306:
+            rec[f"sg_dx_bits_k{k}"] = xx.grad.view(torch.int16).numpy().view(np.uint16)
+        rec[f"sg_out_is_x_k{k}"] = np.array(bool(torch.equal(out.detach(), x)))
+        # exact-k semantics: the reference's CPU STE path
+        y, m = T._torch_wta_forward(x, k)
+        rec[f"exact_mask_k{k}"] = np.packbits(m.numpy(), axis=-1, bitorder="little")
+        if k == 306:
+            rec[f"exact_y_bits_k{k}"] = y.view(torch.int16).numpy().view(np.uint16)
+    np.savez_compressed(os.path.join(HERE, "wta_gelu_48x3072.npz"), **rec)
+    print("wrote wta")
+
+
+def make_k_table(ref):
+    import patch_whisper_sparse_grad as S
+    logits = np.concatenate([np.linspace(-6, 6, 241), [-2.2, -2.1972246, 0.0,
+                             -0.4054651, 2.0]]).astype(np.float32)
+    rows = []
+    for d_ff in (3072, 768, 100):
+        for lg in logits:
+            lk = S.LearnableKRatio(0.4)
+            torch.nn.init.constant_(lk.logit_k, float(lg))
+            rows.append((float(lg), d_ff, lk.get_k(d_ff)))
+    inits = np.array([0.05, 0.1, 0.25, 0.4, 0.5, 0.9, 0.95])
+    init_logits = []
+    for r in inits:
+        lk = S.LearnableKRatio(float(r))
+        init_logits.append(float(lk.logit_k.item()))
+    np.savez_compressed(os.path.join(HERE, "k_table.npz"),
+                        logit=np.array([r[0] for r in rows], dtype=np.float32),
+                        d_ff=np.array([r[1] for r in rows]),
+                        k=np.array([r[2] for r in rows]),
+                        init_ratio=inits, init_logit=np.array(init_logits, dtype=np.float32))
+    print("wrote k_table")
+
+
+def main(argv):
+    ref = _ref_path(argv)
+    sys.path.insert(0, os.path.join(ref, "echo"))
+    torch.set_num_threads(4)
+    make_attn(ref)
+    make_wta(ref)
+    make_k_table(ref)
+
+
+if __name__ == "__main__":
+    main(sys.argv)
