@@ -1,0 +1,185 @@
+/*
+ * tau_dxb.h -- C ABI of the B200 (sm_100a) kernels behind tau-dxb's two
+ * training hot paths: tau-opus attention and WTA top-k sparsity.
+ *
+ * Conventions
+ *   - Every tensor pointer is a DEVICE pointer owned by the caller; the
+ *     library never allocates device memory except where a function says so.
+ *   - Strides are in ELEMENTS, ordered (B, H, L, D) for attention tensors.
+ *     A broadcast mask dimension has stride 0.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *   - Functions return 0 (TAU_DXB_OK) or a negative status; they never throw.
+ *     tau_dxb_last_error() gives a message for the calling thread's last error.
+ *   - All work is asynchronous on `stream`; nothing synchronises the host.
+ *
+ * The reference (inkamrais-hub/tau-dxb) is pure Python; each entry point names
+ * the reference function it replaces (path:line inside that project).
+ */
+#ifndef TAU_DXB_H
+#define TAU_DXB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TAU_DXB_API __attribute__((visibility("default")))
+#else
+#define TAU_DXB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define TAU_DXB_OK                    0
+#define TAU_DXB_ERR_INVALID_ARGUMENT (-1)
+#define TAU_DXB_ERR_UNSUPPORTED      (-2)
+#define TAU_DXB_ERR_CUDA             (-3)
+#define TAU_DXB_ERR_WORKSPACE        (-4)
+#define TAU_DXB_ERR_NO_DEVICE        (-5)
+
+/* ---- element types ----------------------------------------------------- */
+#define TAU_DXB_F32  0
+#define TAU_DXB_BF16 1
+#define TAU_DXB_F16  2
+
+/* ---- sigma ids: same numbering as the reference's _SIGMA_NAME_TO_ID
+ *      (echo/stau_opus_flash_v2.py:400) ---------------------------------- */
+#define TAU_DXB_SIGMA_SOFTPLUS 0
+#define TAU_DXB_SIGMA_SIGMOID  1
+#define TAU_DXB_SIGMA_EXP      2
+#define TAU_DXB_SIGMA_RELU     3
+
+/* ---- attention kernel path ---------------------------------------------- */
+#define TAU_DXB_PATH_AUTO    0  /* tensor cores when supported, else precise */
+#define TAU_DXB_PATH_PRECISE 1  /* fp32 CUDA-core math and accumulation */
+#define TAU_DXB_PATH_TENSOR  2  /* tcgen05/TMEM + TMA; error if unsupported */
+
+/* ---- WTA modes ------------------------------------------------------------ */
+#define TAU_DXB_WTA_THRESHOLD 0 /* keep x >= k-th largest (ties keep more) */
+#define TAU_DXB_WTA_EXACT_K   1 /* keep exactly k; ties by lowest index    */
+
+/* Library version (major*10000 + minor*100 + patch). */
+TAU_DXB_API int tau_dxb_version(void);
+
+/* Static message for a status code. */
+TAU_DXB_API const char* tau_dxb_strerror(int status);
+
+/* Message describing the calling thread's most recent failure ("" if none). */
+TAU_DXB_API const char* tau_dxb_last_error(void);
+
+/*
+ * tau-opus attention forward.
+ * Replaces STauOpusAttentionFunction.forward (echo/stau_opus_operator.py:66-111)
+ * and STauOpusFlashV2Function.forward (echo/stau_opus_flash_v2.py:406-463).
+ *
+ *   s = scale * Q K^T (+ mask) (+ causal: finfo(float).min where j > i + Lk - Lq)
+ *   m = rowmax s, amax = first argmax,  sig = max(sigma(alpha (s - m)), 1e-8)
+ *   q = max(sig^tau, 1e-8),  Z = max(sum q, 1e-8),  out = (q V) / Z
+ *
+ * tau, alpha: fp32 [H], the per-head VALUES. The reference parametrises them
+ *       as tau = softplus(log_tau) + 1 and alpha = exp(log_alpha), computed in
+ *       the parameter's dtype (echo/stau_opus_operator.py:90-91); the caller
+ *       evaluates that and passes the results.
+ * q/k/v/out: `dtype` elements, [B,H,Lq|Lk,D] addressed through the strides.
+ * mask: optional additive mask of `mask_dtype`, indexed (b,h,i,j) through
+ *       mask_stride (0 strides broadcast). May be combined with `causal`.
+ * row_max, row_z: fp32 [B*H*Lq]; row_argmax: int32 [B*H*Lq] (contiguous,
+ *       index (b*H + h)*Lq + i) -- the state the backward needs.
+ * D must be <= 64 (the tensor path needs D == 64 and bf16/f16).
+ */
+TAU_DXB_API int tau_attn_fwd(const void* q, const int64_t q_stride[4],
+                 const void* k, const int64_t k_stride[4],
+                 const void* v, const int64_t v_stride[4],
+                 int32_t dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                 const float* tau, const float* alpha,
+                 int32_t sigma_id, float scale,
+                 const void* mask, int32_t mask_dtype, const int64_t mask_stride[4],
+                 int32_t causal,
+                 void* out, const int64_t out_stride[4],
+                 float* row_max, float* row_z, int32_t* row_argmax,
+                 int32_t path, void* stream);
+
+/* Bytes of device workspace tau_attn_bwd needs for this problem. */
+TAU_DXB_API size_t tau_attn_bwd_workspace_bytes(int64_t B, int64_t H, int64_t Lq, int64_t Lk,
+                                    int64_t D);
+
+/*
+ * tau-opus attention backward.
+ * Replaces STauOpusAttentionFunction.backward (echo/stau_opus_operator.py:113-166)
+ * and STauOpusFlashV2Function.backward (echo/stau_opus_flash_v2.py:466-551).
+ *
+ * Takes the forward's inputs, its output `out` and the upstream gradient
+ * `dout`, plus row_max/row_z/row_argmax from tau_attn_fwd. Writes dq, dk, dv
+ * (`dtype`, strided) and the per-head sums dtau, dalpha (fp32 [H],
+ * overwritten):
+ *   dtau[h]   = sum P (dP - D) max(log sig, -30)
+ *   dalpha[h] = sum tau P (dP - D) clip(sig'/sig * (s - m), -30, 30)
+ * The caller applies the parametrisation's chain rule
+ * (dlog_tau = dtau * sigmoid(log_tau), dlog_alpha = dalpha * exp(log_alpha),
+ * echo/stau_opus_operator.py:154-161).
+ * `workspace` must hold tau_attn_bwd_workspace_bytes(...) bytes of device
+ * memory (256-byte aligned); its contents on entry do not matter.
+ */
+TAU_DXB_API int tau_attn_bwd(const void* q, const int64_t q_stride[4],
+                 const void* k, const int64_t k_stride[4],
+                 const void* v, const int64_t v_stride[4],
+                 const void* out, const int64_t out_stride[4],
+                 const void* dout, const int64_t dout_stride[4],
+                 int32_t dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                 const float* tau, const float* alpha,
+                 int32_t sigma_id, float scale,
+                 const void* mask, int32_t mask_dtype, const int64_t mask_stride[4],
+                 int32_t causal,
+                 const float* row_max, const float* row_z, const int32_t* row_argmax,
+                 void* dq, const int64_t dq_stride[4],
+                 void* dk, const int64_t dk_stride[4],
+                 void* dv, const int64_t dv_stride[4],
+                 float* dtau, float* dalpha,
+                 void* workspace, size_t workspace_bytes,
+                 int32_t path, void* stream);
+
+/*
+ * WTA forward: per-row top-k selection over the last dimension.
+ * Replaces _triton_wta_forward / _WTAFusedSTE.forward (echo/triton_wta.py:71-100),
+ * _torch_wta_forward (echo/triton_wta.py:117-123) and the mask of
+ * SparseGradWTA_Function.forward (echo/patch_whisper_sparse_grad.py:45-55).
+ *
+ * x: [n_rows, d] of `dtype`, rows `row_stride` elements apart.
+ * k: number of winners; if k_dev is non-NULL the kernel reads k from that
+ *    device int32 instead (no host round trip). k is clamped to [1, d].
+ * mode: TAU_DXB_WTA_THRESHOLD or TAU_DXB_WTA_EXACT_K.
+ * y: optional [n_rows, d] contiguous output y = keep ? x : 0 (NULL: mask only,
+ *    the sparse_grad identity forward).
+ * bitmask: [n_rows, (d+7)/8] bytes, bit (j%8) of byte j/8 = keep[j].
+ * win_counts: optional int32 [d]; each kept element adds 1 to its column.
+ */
+TAU_DXB_API int wta_fwd(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_t row_stride,
+            int64_t k, const int32_t* k_dev, int32_t mode,
+            void* y, uint8_t* bitmask, int32_t* win_counts, void* stream);
+
+/*
+ * WTA backward (straight-through): dx = dy * keep.
+ * Replaces _wta_backward_kernel / _WTAFusedSTE.backward (echo/triton_wta.py:53-68,
+ * 102-114) and SparseGradWTA_Function.backward
+ * (echo/patch_whisper_sparse_grad.py:57-60).
+ * dy, dx: contiguous [n_rows, d] of `dtype` (may alias); bitmask as wta_fwd.
+ */
+TAU_DXB_API int wta_bwd(const void* dy, int32_t dtype, const uint8_t* bitmask,
+            int64_t n_rows, int64_t d, void* dx, void* stream);
+
+/*
+ * k for every learnable-k layer at once, on the device:
+ *   k[i] = clamp(round_half_even(sigmoid(logit[i]) * d_ff), 1, d_ff)
+ * Replaces LearnableKRatio.get_k (echo/patch_whisper_sparse_grad.py:159-161)
+ * without its per-layer .item() host sync. logits: fp32 [n]; k_out: int32 [n].
+ */
+TAU_DXB_API int wta_k_from_logits(const float* logits, int64_t n, int64_t d_ff, int32_t* k_out,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TAU_DXB_H */

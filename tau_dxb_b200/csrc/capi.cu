@@ -1,0 +1,218 @@
+// C ABI entry points (include/tau_dxb.h): argument validation, dispatch, errors.
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "attn.h"
+
+namespace taudxb {
+
+namespace {
+thread_local char g_last_error[512] = "";
+}
+
+void set_last_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TAU_DXB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return TAU_DXB_OK;
+}
+
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+int wta_fwd_impl(const void*, int32_t, int64_t, int64_t, int64_t, int64_t, const int32_t*, int32_t,
+                 void*, uint8_t*, int32_t*, cudaStream_t);
+int wta_bwd_impl(const void*, int32_t, const uint8_t*, int64_t, int64_t, void*, cudaStream_t);
+int wta_k_from_logits_impl(const float*, int64_t, int64_t, int32_t*, cudaStream_t);
+
+namespace {
+
+bool valid_dtype(int32_t d) { return d == TAU_DXB_F32 || d == TAU_DXB_BF16 || d == TAU_DXB_F16; }
+
+int fill_common(AttnProblem& p, const void* q, const int64_t* qs, const void* k, const int64_t* ks,
+                const void* v, const int64_t* vs, int32_t dtype, int64_t B, int64_t H, int64_t Lq,
+                int64_t Lk, int64_t D, const float* tau, const float* alpha, int32_t sigma,
+                float scale, const void* mask, int32_t mask_dtype, const int64_t* ms, int32_t causal) {
+  memset(&p, 0, sizeof(p));
+  TDX_CHECK_ARG(q && k && v && qs && ks && vs, "attention: q, k, v and their strides are required");
+  TDX_CHECK_ARG(tau && alpha, "attention: tau and alpha are required");
+  TDX_CHECK_ARG(valid_dtype(dtype), "attention: bad dtype %d", dtype);
+  TDX_CHECK_ARG(B >= 0 && H >= 1 && Lq >= 0 && Lk >= 1 && D >= 1,
+                "attention: bad shape B=%lld H=%lld Lq=%lld Lk=%lld D=%lld",
+                (long long)B, (long long)H, (long long)Lq, (long long)Lk, (long long)D);
+  TDX_CHECK_ARG(B < (1 << 16) && H < (1 << 16) && Lq < (1 << 24) && Lk < (1 << 24) && D <= 128,
+                "attention: shape too large (need B,H < 65536, L < 2^24, D <= 128)");
+  TDX_CHECK_ARG(sigma >= TAU_DXB_SIGMA_SOFTPLUS && sigma <= TAU_DXB_SIGMA_RELU, "attention: bad sigma id %d", sigma);
+  TDX_CHECK_ARG(!mask || (ms && valid_dtype(mask_dtype)), "attention: mask needs strides and a valid dtype");
+  p.q = q; p.k = k; p.v = v;
+  memcpy(p.qs, qs, sizeof(p.qs)); memcpy(p.ks, ks, sizeof(p.ks)); memcpy(p.vs, vs, sizeof(p.vs));
+  p.dtype = dtype;
+  p.B = (int)B; p.H = (int)H; p.Lq = (int)Lq; p.Lk = (int)Lk; p.D = (int)D;
+  p.tau = tau; p.alpha = alpha;
+  p.sigma = sigma; p.scale = scale;
+  p.mask = mask; p.mask_dtype = mask_dtype;
+  if (mask) memcpy(p.ms, ms, sizeof(p.ms));
+  p.causal = causal ? 1 : 0;
+  return TAU_DXB_OK;
+}
+
+bool use_tensor(const AttnProblem& p, int32_t path, int* rc) {
+  *rc = TAU_DXB_OK;
+  if (path == TAU_DXB_PATH_PRECISE) return false;
+  const bool ok = attn_tensor_supported(p);
+  if (path == TAU_DXB_PATH_TENSOR && !ok)
+    *rc = fail(TAU_DXB_ERR_UNSUPPORTED, "tensor-core attention path needs bf16/f16, D == 64 and 16-byte aligned rows with unit d-stride");
+  return ok;
+}
+
+}  // namespace
+}  // namespace taudxb
+
+using namespace taudxb;
+
+extern "C" {
+
+int tau_dxb_version(void) { return 100; }
+
+const char* tau_dxb_strerror(int status) {
+  switch (status) {
+    case TAU_DXB_OK: return "ok";
+    case TAU_DXB_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case TAU_DXB_ERR_UNSUPPORTED: return "unsupported problem";
+    case TAU_DXB_ERR_CUDA: return "CUDA error";
+    case TAU_DXB_ERR_WORKSPACE: return "workspace too small";
+    case TAU_DXB_ERR_NO_DEVICE: return "no CUDA device";
+    default: return "unknown status";
+  }
+}
+
+const char* tau_dxb_last_error(void) { return g_last_error; }
+
+int tau_attn_fwd(const void* q, const int64_t q_stride[4], const void* k, const int64_t k_stride[4],
+                 const void* v, const int64_t v_stride[4], int32_t dtype, int64_t B, int64_t H,
+                 int64_t Lq, int64_t Lk, int64_t D, const float* tau, const float* alpha,
+                 int32_t sigma_id, float scale, const void* mask, int32_t mask_dtype,
+                 const int64_t mask_stride[4], int32_t causal, void* out, const int64_t out_stride[4],
+                 float* row_max, float* row_z, int32_t* row_argmax, int32_t path, void* stream) {
+  g_last_error[0] = 0;
+  AttnProblem p;
+  int rc = fill_common(p, q, q_stride, k, k_stride, v, v_stride, dtype, B, H, Lq, Lk, D, tau,
+                       alpha, sigma_id, scale, mask, mask_dtype, mask_stride, causal);
+  if (rc) return rc;
+  TDX_CHECK_ARG(out && out_stride && row_max && row_z && row_argmax, "tau_attn_fwd: outputs are required");
+  TDX_CHECK_ARG(path >= TAU_DXB_PATH_AUTO && path <= TAU_DXB_PATH_TENSOR, "tau_attn_fwd: bad path %d", path);
+  p.out = out; memcpy(p.outs, out_stride, sizeof(p.outs));
+  p.row_max = row_max; p.row_z = row_z; p.row_argmax = row_argmax;
+  if (B == 0 || Lq == 0) return TAU_DXB_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool tc = use_tensor(p, path, &rc);
+  if (rc) return rc;
+  return tc ? attn_fwd_tensor(p, st) : attn_fwd_precise(p, st);
+}
+
+size_t tau_attn_bwd_workspace_bytes(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D) {
+  if (B < 0 || H < 0 || Lq < 0 || Lk < 0 || D < 0) return 0;
+  return workspace_layout(B, H, Lq, Lk, D).total;
+}
+
+int tau_attn_bwd(const void* q, const int64_t q_stride[4], const void* k, const int64_t k_stride[4],
+                 const void* v, const int64_t v_stride[4], const void* out, const int64_t out_stride[4],
+                 const void* dout, const int64_t dout_stride[4], int32_t dtype, int64_t B, int64_t H,
+                 int64_t Lq, int64_t Lk, int64_t D, const float* tau, const float* alpha,
+                 int32_t sigma_id, float scale, const void* mask, int32_t mask_dtype,
+                 const int64_t mask_stride[4], int32_t causal, const float* row_max,
+                 const float* row_z, const int32_t* row_argmax, void* dq, const int64_t dq_stride[4],
+                 void* dk, const int64_t dk_stride[4], void* dv, const int64_t dv_stride[4],
+                 float* dtau, float* dalpha, void* workspace, size_t workspace_bytes,
+                 int32_t path, void* stream) {
+  g_last_error[0] = 0;
+  AttnProblem p;
+  int rc = fill_common(p, q, q_stride, k, k_stride, v, v_stride, dtype, B, H, Lq, Lk, D, tau,
+                       alpha, sigma_id, scale, mask, mask_dtype, mask_stride, causal);
+  if (rc) return rc;
+  TDX_CHECK_ARG(out && out_stride && dout && dout_stride, "tau_attn_bwd: out and dout are required");
+  TDX_CHECK_ARG(row_max && row_z && row_argmax, "tau_attn_bwd: forward row state is required");
+  TDX_CHECK_ARG(dq && dq_stride && dk && dk_stride && dv && dv_stride && dtau && dalpha,
+                "tau_attn_bwd: gradient outputs are required");
+  TDX_CHECK_ARG(path >= TAU_DXB_PATH_AUTO && path <= TAU_DXB_PATH_TENSOR, "tau_attn_bwd: bad path %d", path);
+  const WorkspaceLayout w = workspace_layout(B, H, Lq, Lk, D);
+  if (!workspace || workspace_bytes < w.total)
+    return fail(TAU_DXB_ERR_WORKSPACE, "tau_attn_bwd: workspace needs %zu bytes, got %zu", w.total, workspace_bytes);
+  TDX_CHECK_ARG(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "tau_attn_bwd: workspace must be 256-byte aligned");
+  p.o = out; memcpy(p.os, out_stride, sizeof(p.os));
+  p.dout = dout; memcpy(p.dos, dout_stride, sizeof(p.dos));
+  p.row_max = const_cast<float*>(row_max); p.row_z = const_cast<float*>(row_z);
+  p.row_argmax = const_cast<int32_t*>(row_argmax);
+  p.dq = dq; memcpy(p.dqs, dq_stride, sizeof(p.dqs));
+  p.dk = dk; memcpy(p.dks, dk_stride, sizeof(p.dks));
+  p.dv = dv; memcpy(p.dvs, dv_stride, sizeof(p.dvs));
+  p.dtau = dtau; p.dalpha = dalpha;
+  char* ws = static_cast<char*>(workspace);
+  p.ws_dq = reinterpret_cast<float*>(ws + w.dq);
+  p.ws_dk = reinterpret_cast<float*>(ws + w.dk);
+  p.ws_drow = reinterpret_cast<float*>(ws + w.drow);
+  p.ws_rowf = reinterpret_cast<float*>(ws + w.rowf);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0 || Lq == 0) {
+    // no query rows: every gradient is zero
+    TDX_CUDA(cudaMemsetAsync(p.dtau, 0, H * sizeof(float), st));
+    TDX_CUDA(cudaMemsetAsync(p.dalpha, 0, H * sizeof(float), st));
+    TDX_CUDA(cudaMemsetAsync(p.ws_dk, 0, w.drow - w.dk, st));
+    p.Lq = 0;
+    return attn_bwd_epilogue(p, st);
+  }
+  const bool tc = use_tensor(p, path, &rc);
+  if (rc) return rc;
+  rc = attn_bwd_prologue(p, st);
+  if (rc) return rc;
+  rc = tc ? attn_bwd_tensor_main(p, st) : attn_bwd_precise_main(p, st);
+  if (rc) return rc;
+  return attn_bwd_epilogue(p, st);
+}
+
+int wta_fwd(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_t row_stride, int64_t k,
+            const int32_t* k_dev, int32_t mode, void* y, uint8_t* bitmask, int32_t* win_counts,
+            void* stream) {
+  g_last_error[0] = 0;
+  return wta_fwd_impl(x, dtype, n_rows, d, row_stride, k, k_dev, mode, y, bitmask, win_counts,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int wta_bwd(const void* dy, int32_t dtype, const uint8_t* bitmask, int64_t n_rows, int64_t d,
+            void* dx, void* stream) {
+  g_last_error[0] = 0;
+  return wta_bwd_impl(dy, dtype, bitmask, n_rows, d, dx, static_cast<cudaStream_t>(stream));
+}
+
+int wta_k_from_logits(const float* logits, int64_t n, int64_t d_ff, int32_t* k_out, void* stream) {
+  g_last_error[0] = 0;
+  return wta_k_from_logits_impl(logits, n, d_ff, k_out, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,166 @@
+"""tau-opus attention kernels against the oracle and the reference's golden
+vectors. fp32 inputs: 1e-4 max relative error; bf16 inputs: 2e-2."""
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, rel_err
+from oracle import stau_attention as OA
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL_FP32 = 1e-4
+TOL_BF16 = 2e-2
+NAMES = ["out", "dQ", "dK", "dV", "dlog_tau", "dlog_alpha"]
+
+
+@pytest.fixture(scope="module")
+def A():
+    from tau_dxb_b200 import attention
+    return attention
+
+
+def run_op(A, Q, K, V, log_tau, log_alpha, sigma, dO, mask=None, scale=None, path="auto",
+           causal_fn=False):
+    """Run forward+backward through the autograd Function; numpy fp32 results."""
+    q, k, v = (t.detach().clone().to(DEV).requires_grad_() for t in (Q, K, V))
+    lt = log_tau.detach().clone().to(DEV).requires_grad_()
+    la = log_alpha.detach().clone().to(DEV).requires_grad_()
+    with A.attention_path(path):
+        if causal_fn:
+            out = A.STauOpusCausalFunction.apply(q, k, v, lt, la, sigma, scale)
+        else:
+            out, none = A.STauOpusAttentionFunction.apply(
+                q, k, v, lt, la, sigma, None if mask is None else mask.to(DEV), scale)
+            assert none is None
+        out.backward(dO.to(DEV).to(out.dtype))
+    torch.cuda.synchronize()
+    f = lambda t: t.detach().float().cpu().numpy()
+    return [f(out), f(q.grad), f(k.grad), f(v.grad), f(lt.grad), f(la.grad)]
+
+
+def oracle(Q, K, V, log_tau, log_alpha, sigma, dO, mask=None, scale=None):
+    f = lambda t: None if t is None else t.detach().float().cpu().numpy()
+    out, grads, _ = OA.forward_backward(f(Q), f(K), f(V), f(log_tau), f(log_alpha), sigma,
+                                        f(dO), f(mask), scale)
+    return [out, *grads]
+
+
+def assert_close(mine, ref, tol, label=""):
+    for n, a, b in zip(NAMES, mine, ref):
+        e = rel_err(a, b)
+        assert e < tol, f"{label} {n}: rel err {e:.3e} >= {tol}"
+
+
+def make_inputs(B, H, Lq, Lk, D=64, seed=0, dtype=torch.float32, lt_std=0.5, la_std=0.0):
+    g = torch.Generator().manual_seed(seed)
+    Q = torch.randn(B, H, Lq, D, generator=g).to(dtype)
+    K = torch.randn(B, H, Lk, D, generator=g).to(dtype)
+    V = torch.randn(B, H, Lk, D, generator=g).to(dtype)
+    dO = torch.randn(B, H, Lq, D, generator=g).to(dtype)
+    lt = torch.randn(H, generator=g) * lt_std
+    la = torch.randn(H, generator=g) * la_std
+    return Q, K, V, lt, la, dO
+
+
+def assert_no_near_ties(Q, K, scale, mask=None, min_gap=1e-4):
+    gap = OA.row_top2_gap(Q.float().numpy(), K.float().numpy(), scale,
+                          None if mask is None else mask.numpy())
+    assert gap > min_gap, f"seeded inputs have a near-tied row max (gap {gap})"
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(GOLDEN, "attn_*.npz"))),
+                         ids=lambda p: os.path.basename(p)[:-4])
+def test_precise_path_matches_reference_golden(A, path):
+    z = np.load(path)
+    t = lambda n: torch.from_numpy(z[n])
+    scale = float(z["scale"])
+    scale = None if np.isnan(scale) else scale
+    mask = t("mask") if "mask" in z.files else None
+    mine = run_op(A, t("Q"), t("K"), t("V"), t("log_tau"), t("log_alpha"), str(z["sigma"]),
+                  t("dO"), mask, scale, path="precise")
+    ref = [z[n] for n in NAMES]
+    assert_close(mine, ref, TOL_FP32, os.path.basename(path))
+
+
+@pytest.mark.parametrize("sigma,causal", [("softplus", False), ("sigmoid", True), ("exp", False),
+                                          ("relu", False)])
+@pytest.mark.parametrize("Lq,Lk", [(1, 1), (63, 63), (65, 129), (127, 64), (200, 200)])
+def test_precise_fp32_shapes(A, sigma, causal, Lq, Lk):
+    Q, K, V, lt, la, dO = make_inputs(2, 3, Lq, Lk, seed=Lq * 1000 + Lk, la_std=0.2)
+    mask = torch.from_numpy(OA.causal_mask(Lq, Lk)) if causal else None
+    assert_no_near_ties(Q, K, 0.125, mask)
+    mine = run_op(A, Q, K, V, lt, la, sigma, dO, mask, None, path="precise")
+    ref = oracle(Q, K, V, lt, la, sigma, dO, mask, None)
+    assert_close(mine, ref, TOL_FP32, f"{sigma} {Lq}x{Lk}")
+
+
+def test_causal_function_equals_mask_tensor(A):
+    Q, K, V, lt, la, dO = make_inputs(2, 4, 70, 70, seed=9)
+    mask = torch.from_numpy(OA.causal_mask(70, 70))
+    a = run_op(A, Q, K, V, lt, la, "sigmoid", dO, mask, 1.0, path="precise")
+    b = run_op(A, Q, K, V, lt, la, "sigmoid", dO, None, 1.0, path="precise", causal_fn=True)
+    for x, y in zip(a, b):
+        assert rel_err(x, y) < 1e-6
+
+
+@pytest.mark.parametrize("sigma,causal,Lq,Lk", [("softplus", False, 300, 300),
+                                                ("sigmoid", True, 200, 200),
+                                                ("exp", False, 96, 300)])
+def test_bf16_auto_path_vs_fp32_oracle(A, sigma, causal, Lq, Lk):
+    Q, K, V, lt, la, dO = make_inputs(2, 4, Lq, Lk, seed=Lq + Lk, dtype=torch.bfloat16)
+    mask = torch.from_numpy(OA.causal_mask(Lq, Lk)) if causal else None
+    scale = 0.125 if sigma == "softplus" else 1.0 / 8
+    assert_no_near_ties(Q, K, scale, mask)
+    mine = run_op(A, Q, K, V, lt, la, sigma, dO, mask, scale, path="auto")
+    ref = oracle(Q, K, V, lt, la, sigma, dO, mask, scale)
+    assert_close(mine, ref, TOL_BF16, f"bf16 {sigma}")
+
+
+def test_tau1_exp_equals_softmax_on_gpu(A):
+    Q, K, V, _, la, dO = make_inputs(2, 4, 100, 150, seed=4)
+    lt = torch.full((4,), -30.0)
+    out = run_op(A, Q, K, V, lt, la, "exp", dO, None, None, path="precise")[0]
+    s = (Q @ K.transpose(-1, -2)) * 0.125
+    ref = (torch.softmax(s, -1) @ V).numpy()
+    assert rel_err(out, ref) < 1e-5
+
+
+def test_noncontiguous_inputs(A):
+    # q/k/v as transposed views of [B, L, H, D] buffers, like the Whisper projections
+    g = torch.Generator().manual_seed(6)
+    Qb, Kb, Vb, dOb = (torch.randn(2, 90, 3, 64, generator=g) for _ in range(4))
+    Q, K, V, dO = (t.transpose(1, 2) for t in (Qb, Kb, Vb, dOb))
+    lt = torch.randn(3, generator=g) * 0.5
+    la = torch.zeros(3)
+    q, k, v = (t.to(DEV).detach().requires_grad_() for t in (Qb, Kb, Vb))
+    lt_d, la_d = lt.to(DEV).requires_grad_(), la.to(DEV).requires_grad_()
+    with A.attention_path("precise"):
+        out, _ = A.STauOpusAttentionFunction.apply(q.transpose(1, 2), k.transpose(1, 2),
+                                                   v.transpose(1, 2), lt_d, la_d, "softplus")
+        out.backward(dO.to(DEV))
+    ref = oracle(Q, K, V, lt, la, "softplus", dO)
+    mine = [out.detach().cpu().numpy(), q.grad.transpose(1, 2).cpu().numpy(),
+            k.grad.transpose(1, 2).cpu().numpy(), v.grad.transpose(1, 2).cpu().numpy(),
+            lt_d.grad.cpu().numpy(), la_d.grad.cpu().numpy()]
+    assert_close(mine, ref, TOL_FP32, "strided")
+
+
+def test_errors(A):
+    Q, K, V, lt, la, dO = make_inputs(1, 2, 8, 8)
+    with pytest.raises(KeyError):
+        A.STauOpusAttentionFunction.apply(Q.to(DEV), K.to(DEV), V.to(DEV), lt.to(DEV),
+                                          la.to(DEV), "nope")
+    with pytest.raises(RuntimeError):
+        A.STauOpusAttentionFunction.apply(Q, K, V, lt, la, "softplus")
+
+
+def test_module_api(A):
+    m = A.STauOpusAttentionModule(4, "softplus").to(DEV)
+    assert [n for n, _ in m.named_parameters()] == ["log_tau", "log_alpha"]
+    Q, K, V, *_ = make_inputs(1, 4, 16, 16)
+    out = m(Q.to(DEV), K.to(DEV), V.to(DEV))
+    assert out.shape == (1, 4, 16, 64)

@@ -1,0 +1,67 @@
+"""The C-ABI library loads without a GPU and exports every declared symbol;
+argument validation answers before any CUDA call."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def _declared_functions():
+    text = open(os.path.join(ROOT, "include", "tau_dxb.h")).read()
+    return sorted(set(re.findall(r"TAU_DXB_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def C():
+    from tau_dxb_b200 import _capi
+    return _capi
+
+
+def test_header_declares_expected_entry_points():
+    names = _declared_functions()
+    for n in ("tau_attn_fwd", "tau_attn_bwd", "tau_attn_bwd_workspace_bytes", "wta_fwd",
+              "wta_bwd", "wta_k_from_logits", "tau_dxb_strerror", "tau_dxb_last_error",
+              "tau_dxb_version"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(C):
+    lib = C.lib()
+    for name in _declared_functions():
+        assert hasattr(lib, name), name
+        assert name in C.SIGNATURES, f"{name} has no ctypes signature"
+    raw = ctypes.CDLL(C.LIB_PATH)
+    for name in _declared_functions():
+        getattr(raw, name)
+
+
+def test_version_and_strerror(C):
+    lib = C.lib()
+    assert lib.tau_dxb_version() >= 100
+    assert C.strerror(0) == "ok"
+    assert C.strerror(C.ERR_WORKSPACE) == "workspace too small"
+    assert C.strerror(12345) == "unknown status"
+
+
+def test_validation_without_gpu(C):
+    lib = C.lib()
+    # missing pointers -> invalid argument, before touching CUDA
+    assert lib.wta_fwd(None, 1, 4, 3072, 3072, 5, None, 0, None, None, None, None) == C.ERR_INVALID_ARGUMENT
+    assert "required" in C.last_error()
+    assert lib.wta_bwd(None, 1, None, 4, 3072, None, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.wta_k_from_logits(None, 3, 3072, None, None) == C.ERR_INVALID_ARGUMENT
+    s = (ctypes.c_int64 * 4)(0, 0, 0, 1)
+    rc = lib.tau_attn_fwd(None, s, None, s, None, s, 1, 1, 1, 8, 8, 64, None, None, 0, 1.0,
+                          None, 0, None, 0, None, s, None, None, None, 0, None)
+    assert rc == C.ERR_INVALID_ARGUMENT
+
+
+def test_workspace_size_formula(C):
+    lib = C.lib()
+    B, H, Lq, Lk, D = 16, 12, 1500, 1500, 64
+    n = lib.tau_attn_bwd_workspace_bytes(B, H, Lq, Lk, D)
+    up = lambda v: (v + 255) // 256 * 256
+    assert n == up(B * H * Lq * D * 4) + up(B * H * Lk * D * 4) + 2 * up(B * H * Lq * 4)
