@@ -27,9 +27,7 @@
 namespace taudxb {
 namespace {
 
-constexpr int kWtaWarps = 8;                 // rows in flight per block
 constexpr int kBins = 257;                   // 256 digit bins + 1 discard bin
-constexpr int kHist8Bytes = kBins * 32;      // u8 counters, [bin][lane]
 constexpr int kHist16Bytes = kBins * 64;     // u16 counters, [bin][lane]
 constexpr uint32_t kFull = 0xffffffffu;
 
@@ -116,8 +114,68 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
 
 // ---------------------------------------------------------------------------
 // Fast path: 16-bit elements, d = 256 * CH, rows 16-byte aligned.
+//
+// Counters: per warp a [257 bins][16 words] u32 array; lane l owns the 16-bit
+// half (l & 1) of word (l >> 1) in every bin row. Updates are fire-and-forget
+// `red.shared.add` (no load-add-store dependency chain through shared memory);
+// only the two lanes sharing a word can collide on one address.
+
+__device__ __forceinline__ void red_shared_add(uint32_t addr, uint32_t v) {
+  asm volatile("red.shared.add.u32 [%0], %1;" :: "r"(addr), "r"(v) : "memory");
+}
+
+// Find the digit bin holding the k-th largest key from u16-pair counters.
+// Lane l owns bins l + 32*j; it sums the 16 words of each of its bins (4
+// staggered 16-byte loads, conflict-free) and zeroes them.
+__device__ __forceinline__ void select_bin_pairs(uint32_t* hist, int lane, int k, int& bstar,
+                                                 int& above_out) {
+  uint32_t cnt[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4* row = reinterpret_cast<uint4*>(hist + (lane + 32 * j) * 16);
+    uint32_t acc = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = (q + (lane >> 1)) & 3;
+      const uint4 a = row[c];
+      acc += a.x + a.y + a.z + a.w;          // two 16-bit fields, each <= d
+      row[c] = make_uint4(0, 0, 0, 0);
+    }
+    cnt[j] = (acc & 0xFFFFu) + (acc >> 16);
+  }
+  int above = 0, jstar = 0;
+  bool found = false;
+#pragma unroll
+  for (int j = 7; j >= 0; --j) {
+    const int g = static_cast<int>(__reduce_add_sync(kFull, cnt[j]));
+    if (!found) {
+      if (above + g >= k) { jstar = j; found = true; }
+      else above += g;
+    }
+  }
+  uint32_t c = cnt[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) if (j == jstar) c = cnt[j];
+  uint32_t s = c;                                // inclusive suffix sum over lanes
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t t = __shfl_down_sync(kFull, s, off);
+    if (lane + off < 32) s += t;
+  }
+  const uint32_t S = s + static_cast<uint32_t>(above);
+  const uint32_t ge = __ballot_sync(kFull, S >= static_cast<uint32_t>(k));
+  const int lstar = 31 - __clz(ge);
+  const uint32_t S_l = __shfl_sync(kFull, S, lstar);
+  const uint32_t c_l = __shfl_sync(kFull, c, lstar);
+  bstar = 32 * jstar + lstar;
+  above_out = static_cast<int>(S_l - c_l);
+}
+
+constexpr int kFastWarps = 4;                    // rows in flight per block
+constexpr int kPairHistBytes = kBins * 64;       // [257][16] u32 per warp
+
 template <int CH, bool EXACT, bool WRITE_Y, bool HIST>
-__global__ void __launch_bounds__(kWtaWarps * 32)
+__global__ void __launch_bounds__(kFastWarps * 32, 3)
 wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_stride,
                  int k_host, const int32_t* __restrict__ k_dev,
                  uint16_t* __restrict__ y, uint8_t* __restrict__ bitmask,
@@ -125,26 +183,40 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
   constexpr int D = 256 * CH;
   extern __shared__ __align__(16) uint8_t smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint8_t* hist = smem + warp * kHist8Bytes;
-  int32_t* shist = reinterpret_cast<int32_t*>(smem + kWtaWarps * kHist8Bytes);
-  for (int i = lane; i < kHist8Bytes / 16; i += 32)
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + warp * kPairHistBytes);
+  int32_t* shist = reinterpret_cast<int32_t*>(smem + kFastWarps * kPairHistBytes);
+  for (int i = lane; i < kPairHistBytes / 16; i += 32)
     reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
   if (HIST)
     for (int i = threadIdx.x; i < D; i += blockDim.x) shist[i] = 0;
   __syncthreads();
   int k = k_dev ? *k_dev : k_host;
   k = max(1, min(D, k));
-  uint8_t* hl = hist + lane;
+  // this lane's counter: word (lane >> 1) of a bin row, 16-bit half (lane & 1)
+  const uint32_t hbase = static_cast<uint32_t>(__cvta_generic_to_shared(hist)) + (lane >> 1) * 4;
+  const uint32_t inc = 1u << ((lane & 1) * 16);
 
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWtaWarps + warp; row < n_rows;
-       row += static_cast<int64_t>(gridDim.x) * kWtaWarps) {
+  const int64_t stride_rows = static_cast<int64_t>(gridDim.x) * kFastWarps;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * kFastWarps + warp;
+  uint4 nxt[CH];
+  if (row < n_rows) {
     const uint4* src = reinterpret_cast<const uint4*>(x + row * row_stride);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) nxt[c] = __ldcs(src + c * 32 + lane);
+  }
+  for (; row < n_rows; row += stride_rows) {
     uint32_t kw[CH][4];
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      const uint4 v = __ldg(src + c * 32 + lane);
-      kw[c][0] = keys16(v.x); kw[c][1] = keys16(v.y);
-      kw[c][2] = keys16(v.z); kw[c][3] = keys16(v.w);
+      kw[c][0] = keys16(nxt[c].x); kw[c][1] = keys16(nxt[c].y);
+      kw[c][2] = keys16(nxt[c].z); kw[c][3] = keys16(nxt[c].w);
+    }
+    // prefetch the next row while this one is selected
+    const int64_t nrow = row + stride_rows;
+    if (nrow < n_rows) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + nrow * row_stride);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) nxt[c] = __ldcs(src + c * 32 + lane);
     }
     // pass 1: high byte of every key
 #pragma unroll
@@ -152,30 +224,28 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint32_t w = kw[c][i];
-        hl[__byte_perm(w, 0, 0x4441) * 32] += 1;
-        hl[(w >> 24) * 32] += 1;
+        red_shared_add(hbase + __byte_perm(w, 0, 0x4441) * 64, inc);
+        red_shared_add(hbase + (w >> 24) * 64, inc);
       }
     __syncwarp();
     int b1, above1;
-    select_bin(hist, lane, k, b1, above1);
+    select_bin_pairs(hist, lane, k, b1, above1);
     __syncwarp();
-    // pass 2: low byte of keys whose high byte is b1 (others -> discard bin)
-    const uint32_t base = static_cast<uint32_t>(b1) << 8;
+    // pass 2: low byte of keys whose high byte is b1; others go to bin 256
+    const uint32_t hb2 = (static_cast<uint32_t>(b1) << 8) | (static_cast<uint32_t>(b1) << 24);
 #pragma unroll
     for (int c = 0; c < CH; ++c)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint32_t w = kw[c][i];
-        const uint32_t d0 = min((w & 0xFFFFu) - base, 256u);
-        const uint32_t d1 = min((w >> 16) - base, 256u);
-        hl[d0 * 32] += 1;
-        hl[d1 * 32] += 1;
+        const uint32_t xw = kw[c][i] ^ hb2;            // matching keys -> high byte 0
+        red_shared_add(hbase + min(xw & 0xFFFFu, 256u) * 64, inc);
+        red_shared_add(hbase + min(xw >> 16, 256u) * 64, inc);
       }
     __syncwarp();
     int b2, above2;
-    select_bin(hist, lane, k - above1, b2, above2);
+    select_bin_pairs(hist, lane, k - above1, b2, above2);
     __syncwarp();
-    const uint32_t t = base | static_cast<uint32_t>(b2);
+    const uint32_t t = (static_cast<uint32_t>(b1) << 8) | static_cast<uint32_t>(b2);
     uint32_t tlo = t, thi = t;
     if (t == 0x8000u || t == 0x7FFFu) { tlo = 0x7FFFu; thi = 0x8000u; }   // +0 == -0
 
@@ -185,9 +255,8 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
 #pragma unroll
       for (int c = 0; c < CH; ++c)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 4; ++i)
           gt += ((kw[c][i] & 0xFFFFu) > thi) + ((kw[c][i] >> 16) > thi);
-        }
       need = k - static_cast<int>(__reduce_add_sync(kFull, static_cast<uint32_t>(gt)));
     }
     uint8_t* mrow = bitmask + row * (D / 8);
@@ -231,7 +300,7 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
           if (EXACT) sel |= 0x80008000u;   // x * 0 keeps the sign
           o[i] = unkeys16(kw[c][i]) & sel;
         }
-        yrow[c * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
+        __stcs(yrow + c * 32 + lane, make_uint4(o[0], o[1], o[2], o[3]));
       }
       if (HIST) {
         const int col0 = (c * 32 + lane) * 8;
@@ -385,15 +454,15 @@ template <int CH, bool EXACT, bool WRITE_Y, bool HIST>
 int launch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, const int32_t* k_dev,
                  void* y, uint8_t* bitmask, int32_t* win, cudaStream_t st) {
   auto kern = wta_fwd16_kernel<CH, EXACT, WRITE_Y, HIST>;
-  const size_t smem = kWtaWarps * kHist8Bytes + (HIST ? 256 * CH * 4 : 0);
+  const size_t smem = kFastWarps * kPairHistBytes + (HIST ? 256 * CH * 4 : 0);
   TDX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
-  TDX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWtaWarps * 32, smem));
+  TDX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFastWarps * 32, smem));
   per_sm = per_sm < 1 ? 1 : per_sm;
-  int64_t blocks = (n_rows + kWtaWarps - 1) / kWtaWarps;
+  int64_t blocks = (n_rows + kFastWarps - 1) / kFastWarps;
   const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm;
   if (blocks > cap) blocks = cap;
-  kern<<<static_cast<unsigned>(blocks), kWtaWarps * 32, smem, st>>>(
+  kern<<<static_cast<unsigned>(blocks), kFastWarps * 32, smem, st>>>(
       static_cast<const uint16_t*>(x), n_rows, row_stride, k, k_dev,
       static_cast<uint16_t*>(y), bitmask, win);
   return check_launch("wta_fwd16_kernel");
