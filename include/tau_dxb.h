@@ -69,6 +69,12 @@ TAU_DXB_API const char* tau_dxb_strerror(int status);
 /* Message describing the calling thread's most recent failure ("" if none). */
 TAU_DXB_API const char* tau_dxb_last_error(void);
 
+/* Device-side error word of the current device (0 = none): bit 1/2/4 = a
+ * tensor-core kernel gave up waiting (TMA / MMA / softmax role) after its
+ * time limit instead of hanging. Synchronises the device; reset != 0 clears
+ * it. Returns -1 if it cannot be read. No reference counterpart (diagnostic). */
+TAU_DXB_API int tau_dxb_device_error(int32_t reset);
+
 /*
  * tau-opus attention forward.
  * Replaces STauOpusAttentionFunction.forward (echo/stau_opus_operator.py:66-111)

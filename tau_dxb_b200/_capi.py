@@ -35,6 +35,7 @@ SIGNATURES = {
     "tau_dxb_version": (ctypes.c_int, []),
     "tau_dxb_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "tau_dxb_last_error": (ctypes.c_char_p, []),
+    "tau_dxb_device_error": (ctypes.c_int, [ctypes.c_int32]),
     "tau_attn_fwd": (ctypes.c_int, [
         _vp, _i64p, _vp, _i64p, _vp, _i64p,           # q, k, v
         _i32, _i64, _i64, _i64, _i64, _i64,           # dtype, B, H, Lq, Lk, D

@@ -47,6 +47,8 @@ int attn_bwd_precise_main(const AttnProblem& p, cudaStream_t st);
 // tensor-core (tcgen05) kernels; return TAU_DXB_ERR_UNSUPPORTED when the
 // problem is outside what they handle.
 bool attn_tensor_supported(const AttnProblem& p);
+bool attn_tensor_bwd_supported(const AttnProblem& p);
+int read_device_error(int reset);
 int attn_fwd_tensor(const AttnProblem& p, cudaStream_t st);
 int attn_bwd_tensor_main(const AttnProblem& p, cudaStream_t st);
 

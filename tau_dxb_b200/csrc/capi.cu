@@ -82,10 +82,10 @@ int fill_common(AttnProblem& p, const void* q, const int64_t* qs, const void* k,
   return TAU_DXB_OK;
 }
 
-bool use_tensor(const AttnProblem& p, int32_t path, int* rc) {
+bool use_tensor(const AttnProblem& p, int32_t path, int* rc, bool bwd) {
   *rc = TAU_DXB_OK;
   if (path == TAU_DXB_PATH_PRECISE) return false;
-  const bool ok = attn_tensor_supported(p);
+  const bool ok = bwd ? attn_tensor_bwd_supported(p) : attn_tensor_supported(p);
   if (path == TAU_DXB_PATH_TENSOR && !ok)
     *rc = fail(TAU_DXB_ERR_UNSUPPORTED, "tensor-core attention path needs bf16/f16, D == 64 and 16-byte aligned rows with unit d-stride");
   return ok;
@@ -131,7 +131,7 @@ int tau_attn_fwd(const void* q, const int64_t q_stride[4], const void* k, const 
   p.row_max = row_max; p.row_z = row_z; p.row_argmax = row_argmax;
   if (B == 0 || Lq == 0) return TAU_DXB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool tc = use_tensor(p, path, &rc);
+  const bool tc = use_tensor(p, path, &rc, false);
   if (rc) return rc;
   return tc ? attn_fwd_tensor(p, st) : attn_fwd_precise(p, st);
 }
@@ -187,7 +187,7 @@ int tau_attn_bwd(const void* q, const int64_t q_stride[4], const void* k, const 
     p.Lq = 0;
     return attn_bwd_epilogue(p, st);
   }
-  const bool tc = use_tensor(p, path, &rc);
+  const bool tc = use_tensor(p, path, &rc, true);
   if (rc) return rc;
   rc = attn_bwd_prologue(p, st);
   if (rc) return rc;
@@ -195,6 +195,8 @@ int tau_attn_bwd(const void* q, const int64_t q_stride[4], const void* k, const 
   if (rc) return rc;
   return attn_bwd_epilogue(p, st);
 }
+
+int tau_dxb_device_error(int32_t reset) { return read_device_error(reset); }
 
 int wta_fwd(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_t row_stride, int64_t k,
             const int32_t* k_dev, int32_t mode, void* y, uint8_t* bitmask, int32_t* win_counts,

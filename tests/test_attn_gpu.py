@@ -171,3 +171,68 @@ def test_module_api(A):
     Q, K, V, *_ = make_inputs(1, 4, 16, 16)
     out = m(Q.to(DEV), K.to(DEV), V.to(DEV))
     assert out.shape == (1, 4, 16, 64)
+
+
+# ------------------------------------------------------------ tensor-core forward
+
+def fwd_direct(Q, K, V, lt, la, sigma, scale, path, mask=None, causal=False, layout="blhd"):
+    """Forward through the C ABI only; returns out, row_max, row_z, row_argmax (CPU)."""
+    import torch.nn.functional as F
+    from tau_dxb_b200 import _capi as C
+    B, H, Lq, D = Q.shape
+    Lk = K.shape[2]
+
+    def dev(t):
+        if layout == "blhd":   # [B,H,L,D] view of a [B,L,H,D] buffer, like the Whisper projections
+            return t.transpose(1, 2).contiguous().to(DEV).transpose(1, 2)
+        return t.contiguous().to(DEV)
+    q, k, v = dev(Q), dev(K), dev(V)
+    tau = (F.softplus(lt) + 1).float().to(DEV)
+    alpha = torch.exp(la).float().to(DEV)
+    out = torch.empty(B, Lq, H, D, dtype=Q.dtype, device=DEV).transpose(1, 2)
+    m = torch.empty(B, H, Lq, device=DEV)
+    z = torch.empty_like(m)
+    a = torch.empty(B, H, Lq, dtype=torch.int32, device=DEV)
+    md = None
+    if mask is not None:
+        md = mask.to(DEV).expand(B, H, Lq, Lk)
+    rc = C.lib().tau_attn_fwd(
+        q.data_ptr(), C.strides4(q), k.data_ptr(), C.strides4(k), v.data_ptr(), C.strides4(v),
+        C.dtype_code(Q.dtype), B, H, Lq, Lk, D, tau.data_ptr(), alpha.data_ptr(),
+        C.SIGMA_IDS[sigma], float(scale), md.data_ptr() if md is not None else None,
+        C.F32 if md is not None else 0, C.strides4(md) if md is not None else None, int(causal),
+        out.data_ptr(), C.strides4(out), m.data_ptr(), z.data_ptr(), a.data_ptr(),
+        {"tensor": C.PATH_TENSOR, "precise": C.PATH_PRECISE}[path], C.stream_ptr())
+    C.check("tau_attn_fwd", rc)
+    torch.cuda.synchronize()
+    assert C.lib().tau_dxb_device_error(1) == 0
+    return out.float().cpu().numpy(), m.cpu().numpy(), z.cpu().numpy(), a.cpu().numpy()
+
+
+@pytest.mark.parametrize("sigma,causal,B,H,Lq,Lk", [
+    ("softplus", False, 2, 3, 300, 300), ("softplus", False, 1, 2, 1, 1),
+    ("softplus", False, 1, 2, 128, 128), ("softplus", False, 1, 2, 256, 384),
+    ("sigmoid", True, 2, 2, 200, 200), ("exp", False, 2, 3, 96, 300),
+    ("exp", False, 1, 2, 520, 77), ("relu", False, 1, 2, 64, 64)])
+def test_tensor_forward_vs_oracle(sigma, causal, B, H, Lq, Lk):
+    Q, K, V, lt, la, _ = make_inputs(B, H, Lq, Lk, seed=Lq * 7 + Lk, dtype=torch.bfloat16, la_std=0.2)
+    scale = 0.125
+    mask = torch.from_numpy(OA.causal_mask(Lq, Lk)) if causal else None
+    assert_no_near_ties(Q, K, scale, mask)
+    out, m, z, a = fwd_direct(Q, K, V, lt, la, sigma, scale, "tensor", causal=causal)
+    f = lambda t: t.float().numpy()
+    ref_out, ctx = OA.forward(f(Q), f(K), f(V), f(lt), f(la), sigma,
+                              None if mask is None else mask.numpy(), scale)
+    assert rel_err(out, ref_out) < TOL_BF16, rel_err(out, ref_out)
+    assert np.abs(m - ctx["m"]).max() < 1e-4
+    assert np.array_equal(a, ctx["argmax"])
+    assert rel_err(z, ctx["Z"]) < 1e-3
+
+
+def test_tensor_forward_mask_tensor_and_layouts():
+    Q, K, V, lt, la, _ = make_inputs(2, 2, 150, 150, seed=77, dtype=torch.bfloat16)
+    mask = torch.from_numpy(OA.causal_mask(150, 150))
+    a1 = fwd_direct(Q, K, V, lt, la, "sigmoid", 0.125, "tensor", mask=mask)
+    a2 = fwd_direct(Q, K, V, lt, la, "sigmoid", 0.125, "tensor", causal=True, layout="bhld")
+    for x, y in zip(a1, a2):
+        assert rel_err(x, y) < 1e-6
