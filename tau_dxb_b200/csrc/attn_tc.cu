@@ -437,7 +437,6 @@ bool attn_tensor_supported(const AttnProblem& p) {
   return true;
 }
 
-bool attn_tensor_bwd_supported(const AttnProblem&) { return false; }
 
 int attn_fwd_tensor(const AttnProblem& p, cudaStream_t st) {
   FwdParams fp;
@@ -451,8 +450,8 @@ int attn_fwd_tensor(const AttnProblem& p, cudaStream_t st) {
   fp.mask = p.mask; fp.mask_dtype = p.mask_dtype;
   for (int i = 0; i < 4; ++i) { fp.ms[i] = p.ms[i]; fp.os[i] = p.outs[i]; }
   fp.out = p.out; fp.row_max = p.row_max; fp.row_z = p.row_z; fp.row_argmax = p.row_argmax;
-  int* err = nullptr;
-  TDX_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error_word));
+  int* err = device_error_word();
+  if (!err) return fail(TAU_DXB_ERR_CUDA, "cannot resolve the device error word");
   fp.err = err;
   dim3 grid((p.Lq + 2 * kBM - 1) / (2 * kBM), p.H, p.B);
   auto launch = [&](auto kern) -> int {
@@ -468,8 +467,10 @@ int attn_fwd_tensor(const AttnProblem& p, cudaStream_t st) {
   }
 }
 
-int attn_bwd_tensor_main(const AttnProblem&, cudaStream_t) {
-  return fail(TAU_DXB_ERR_UNSUPPORTED, "tensor-core attention backward not built yet");
+int* device_error_word() {
+  int* err = nullptr;
+  if (cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_error_word) != cudaSuccess) return nullptr;
+  return err;
 }
 
 int read_device_error(int reset) {

@@ -1,0 +1,540 @@
+// tau-opus attention backward, tensor-core path for sm_100a (bf16, D = 64).
+//
+// One CTA owns a 128-key tile of one (b, h) and streams every 128-row query
+// tile through it (K, V loaded once; Q_i, dO_i double-buffered by TMA):
+//   S^T  = K Q_i^T          (M=128 keys, N=128 queries, K=64)   -> TMEM [0,128)
+//   dP^T = V dO_i^T         (M=128,      N=128,         K=64)   -> TMEM [128,256)
+//   elementwise, one thread per key row: P = q / Z and
+//     F = tau alpha P (dP - D) sigma'/sigma   (the reference's d_s_stable before
+//     the argmax shift, echo/stau_opus_operator.py:134-137), written as bf16
+//     P^T and dS^T = F^T tiles in 128B-swizzled shared memory;
+//     dtau / dalpha partial sums stay in registers.
+//   dV  += P^T dO_i         (M=128 keys, N=64, K=128 queries)   -> TMEM [256,320)
+//   dK  += dS^T Q_i                                              -> TMEM [320,384)
+//   dQ_i = dS [K | 1]       (M=128 queries, N=80, K=128 keys)   -> TMEM [384,464)
+//     The dS^T buffer doubles as the MN-major A operand of this MMA, and the
+//     extra all-ones column of B yields rowsum_keys(F) in column 64 -- the
+//     quantity the argmax correction needs.
+//   dQ_i leaves through a TMA bulk reduce-add into the fp32 dQ accumulator;
+//   its rowsum column is added to the rowsum(F) accumulator.
+// Warp roles (16 warps): 0 TMA, 1 MMA + TMEM owner, 2 row statistics of each
+// query tile, 4-7 dQ epilogue (and the final dK / dV store), 8-15 elementwise
+// (two groups of 4 warps, query columns [0,64) and [64,128)).
+// The argmax correction, dK scaling and dtype casts run afterwards in the
+// shared epilogue kernels (attn_common.cu).
+
+#include "attn.h"
+#include "poly_coeffs.h"
+#include "tc_common.cuh"
+
+namespace taudxb {
+
+bool make_tmap_f32_rows64(CUtensorMap* map, void* base, int64_t rows, int64_t planes, int box_rows) {
+  using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !p) {
+      set_last_error("cuTensorMapEncodeTiled is not available from the driver");
+      return false;
+    }
+    fn = reinterpret_cast<EncodeFn>(p);
+  }
+  const cuuint64_t gdim[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(planes)};
+  const cuuint64_t gstride[2] = {64 * 4, static_cast<cuuint64_t>(rows) * 64 * 4};
+  const cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, gdim, gstride, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled (fp32) failed (%d)", static_cast<int>(r));
+    return false;
+  }
+  return true;
+}
+
+namespace {
+
+constexpr int kT = 128, kD = 64, kThreads = 512;
+constexpr uint32_t kTile = kT * kD * 2;       // 16 KB bf16 tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kLog2Clamp = -26.575424759098897f;   // log2(1e-8)
+constexpr int kErrTimeoutTma = 1, kErrTimeoutMma = 2, kErrTimeoutCompute = 4;
+
+struct BwdParams {
+  CUtensorMap tq, tk, tv, tdo, tdq;
+  int B, H, Lq, Lk;
+  const float* tau;
+  const float* alpha;
+  float scale;
+  int causal;
+  const void* mask; int mask_dtype; int64_t ms[4];
+  const float* row_max; const float* row_z; const float* drow;
+  float* ws_rowf; float* ws_dk;
+  void* dv; int64_t dvs[4];
+  float* dtau; float* dalpha;
+  int* err;
+};
+
+struct __align__(8) BwdBarriers {
+  uint64_t kv_full;
+  uint64_t qd_full[2];
+  uint64_t qd_empty[2];
+  uint64_t s_full;
+  uint64_t s_free;
+  uint64_t ds_ready;
+  uint64_t p_free;
+  uint64_t dq_full;
+  uint64_t dq_free;
+  uint64_t fin;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  float red_tau, red_alpha;
+};
+
+constexpr uint32_t kOffK = 0;                       // K tile, then the ones tile (LBO 16 KB)
+constexpr uint32_t kOffOnes = kOffK + kTile;
+constexpr uint32_t kOffV = kOffOnes + kTile;
+constexpr uint32_t kOffQ = kOffV + kTile;           // 2 stages
+constexpr uint32_t kOffDO = kOffQ + 2 * kTile;      // 2 stages
+constexpr uint32_t kOffP = kOffDO + 2 * kTile;      // P^T, 2 atoms of 64 queries
+constexpr uint32_t kOffDS = kOffP + 2 * kTile;      // dS^T, 2 atoms
+constexpr uint32_t kOffStage = kOffDS + 2 * kTile;  // dQ staging, 2 boxes [128][32] fp32
+constexpr uint32_t kOffStats = kOffStage + 2 * kTile;   // 2 stages x {mc, rz, dq} x 128 fp32
+constexpr uint32_t kOffBar = kOffStats + 2 * 3 * kT * 4;
+constexpr uint32_t kBwdSmem = kOffBar + sizeof(BwdBarriers) + 1024;
+
+constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
+
+// log2 sigma and sigma'/sigma for x <= 0 from a2 = x log2(e)
+template <int SIG>
+__device__ __forceinline__ void sigma_terms(float a2, float& lg, float& ratio) {
+  if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
+    const float e = tc::ex2(a2);
+    lg = a2 + poly::G(e);
+    ratio = poly::R(e);
+  } else if (SIG == TAU_DXB_SIGMA_SIGMOID) {
+    const float e = tc::ex2(a2);
+    lg = a2 - poly::H(e);
+    ratio = poly::S(e);
+  } else if (SIG == TAU_DXB_SIGMA_EXP) {
+    lg = a2;
+    ratio = 1.f;
+  } else {
+    lg = kLog2Clamp;
+    ratio = 1.f;
+  }
+  lg = fmaxf(lg, kLog2Clamp);
+}
+
+__device__ __forceinline__ float bwd_mask_value(const BwdParams& p, int b, int h, int r, int c) {
+  float mv = 0.f;
+  if (p.mask) {
+    const int64_t off = b * p.ms[0] + h * p.ms[1] + static_cast<int64_t>(r) * p.ms[2] +
+                        static_cast<int64_t>(c) * p.ms[3];
+    mv = load_as_float(p.mask, p.mask_dtype, off);
+  }
+  if (p.causal && c > r + (p.Lk - p.Lq)) mv += kMaskMin;
+  return mv;
+}
+
+template <int SIG>
+__global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_constant__ BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(smem + kOffBar);
+  float* stats = reinterpret_cast<float*>(smem + kOffStats);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, h = blockIdx.y, k0 = blockIdx.x * kT;
+  const int nQ = (p.Lq + kT - 1) / kT;
+  const int64_t bh = static_cast<int64_t>(b) * p.H + h;
+  volatile int* abort_flag = &bars->abort_flag;
+
+  // the all-ones column (n = 0 of the second B atom of the dQ MMA), MN-major SW128
+  for (int i = threadIdx.x; i < static_cast<int>(kTile / 16); i += kThreads) {
+    const int row = i >> 3, chunk = i & 7;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (chunk == (0 ^ (row & 7))) v.x = 0x3F80u;   // bf16 1.0 in element 0 of logical chunk 0
+    reinterpret_cast<uint4*>(smem + kOffOnes)[i] = v;
+  }
+  tc::fence_async_smem();
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bars->kv_full, 1);
+    for (int s = 0; s < 2; ++s) { tc::mbar_init(&bars->qd_full[s], 2); tc::mbar_init(&bars->qd_empty[s], 1); }
+    tc::mbar_init(&bars->s_full, 1);
+    tc::mbar_init(&bars->s_free, 8);
+    tc::mbar_init(&bars->ds_ready, 8);
+    tc::mbar_init(&bars->p_free, 1);
+    tc::mbar_init(&bars->dq_full, 1);
+    tc::mbar_init(&bars->dq_free, 4);
+    tc::mbar_init(&bars->fin, 1);
+    tc::mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    bars->red_tau = 0.f;
+    bars->red_alpha = 0.f;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) { tc::tmem_alloc(&bars->tmem_base, 512); tc::tmem_relinquish(); }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const float tau = p.tau[h], alpha = p.alpha[h];
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA
+    if (lane == 0) {
+      tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * kTile);
+      tc::tma_load_4d(smem + kOffK, &p.tk, &bars->kv_full, 0, k0, h, b);
+      tc::tma_load_4d(smem + kOffV, &p.tv, &bars->kv_full, 0, k0, h, b);
+      int issued = 0;
+      for (int i = 0; i < nQ; ++i) {
+        const int s = i & 1;
+        if (i >= 2 && !tc::mbar_wait(&bars->qd_empty[s], ((i >> 1) - 1) & 1, abort_flag, p.err, kErrTimeoutTma))
+          break;
+        tc::mbar_arrive_expect_tx(&bars->qd_full[s], 2 * kTile);
+        tc::tma_load_4d(smem + kOffQ + s * kTile, &p.tq, &bars->qd_full[s], 0, i * kT, h, b);
+        tc::tma_load_4d(smem + kOffDO + s * kTile, &p.tdo, &bars->qd_full[s], 0, i * kT, h, b);
+        issued = i + 1;
+      }
+      if (*abort_flag) {   // let started copies land before the CTA exits
+        const uint64_t t0 = tc::globaltimer_ns();
+        for (int i = (issued > 2 ? issued - 2 : 0); i < issued; ++i) {
+          const uint32_t a = tc::smem_u32(&bars->qd_full[i & 1]);
+          while (!tc::mbar_try_wait(a, (i >> 1) & 1) && tc::globaltimer_ns() - t0 < tc::kWaitLimitNs) {
+          }
+        }
+        const uint32_t a = tc::smem_u32(&bars->kv_full);
+        while (!tc::mbar_try_wait(a, 0) && tc::globaltimer_ns() - t0 < tc::kWaitLimitNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idS = tc::idesc_bf16(kT, kT, 0, 0);
+      constexpr uint32_t idG = tc::idesc_bf16(kT, kD, 0, 1);
+      constexpr uint32_t idQ = tc::idesc_bf16(kT, kD + 16, 1, 1);
+      const uint32_t sK = tc::smem_u32(smem + kOffK), sV = tc::smem_u32(smem + kOffV);
+      const uint32_t sQ = tc::smem_u32(smem + kOffQ), sDO = tc::smem_u32(smem + kOffDO);
+      const uint32_t sP = tc::smem_u32(smem + kOffP), sDS = tc::smem_u32(smem + kOffDS);
+      bool ok = tc::mbar_wait(&bars->kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
+      for (int i = 0; i <= nQ && ok; ++i) {
+        if (i < nQ) {
+          const int s = i & 1;
+          ok = tc::mbar_wait(&bars->qd_full[s], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma);
+          if (ok && i > 0) ok = tc::mbar_wait(&bars->s_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
+          if (!ok) break;
+          tc::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            tc::umma_f16_ss(tmem + kColS, tc::sdesc_sw128(sK + kk * 32, 16, 1024),
+                            tc::sdesc_sw128(sQ + s * kTile + kk * 32, 16, 1024), idS, kk > 0);
+          }
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            tc::umma_f16_ss(tmem + kColDP, tc::sdesc_sw128(sV + kk * 32, 16, 1024),
+                            tc::sdesc_sw128(sDO + s * kTile + kk * 32, 16, 1024), idS, kk > 0);
+          }
+          tc::umma_commit(&bars->s_full);
+        }
+        if (i > 0) {
+          const int j = i - 1, sj = j & 1;
+          ok = tc::mbar_wait(&bars->ds_ready, j & 1, abort_flag, p.err, kErrTimeoutMma);
+          if (ok && j > 0) ok = tc::mbar_wait(&bars->dq_free, (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
+          if (!ok) break;
+          tc::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk) {      // dV += P^T dO_j
+            const uint32_t pa = sP + (kk >> 2) * kTile + (kk & 3) * 32;
+            tc::umma_f16_ss(tmem + kColDV, tc::sdesc_sw128(pa, 16, 1024),
+                            tc::sdesc_sw128(sDO + sj * kTile + kk * 2048, 16384, 1024), idG,
+                            (j > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk) {      // dK += dS^T Q_j
+            const uint32_t pa = sDS + (kk >> 2) * kTile + (kk & 3) * 32;
+            tc::umma_f16_ss(tmem + kColDK, tc::sdesc_sw128(pa, 16, 1024),
+                            tc::sdesc_sw128(sQ + sj * kTile + kk * 2048, 16384, 1024), idG,
+                            (j > 0 || kk > 0) ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk) {      // dQ_j = dS [K | 1]
+            tc::umma_f16_ss(tmem + kColDQ, tc::sdesc_sw128(sDS + kk * 2048, 16384, 1024),
+                            tc::sdesc_sw128(sK + kk * 2048, 16384, 1024), idQ, kk > 0);
+          }
+          tc::umma_commit(&bars->p_free);
+          tc::umma_commit(&bars->qd_empty[sj]);
+          tc::umma_commit(&bars->dq_full);
+        }
+      }
+      tc::umma_commit(&bars->fin);
+      tc::umma_commit(&bars->drain);
+      const uint64_t t0 = tc::globaltimer_ns();
+      const uint32_t a = tc::smem_u32(&bars->drain);
+      while (!tc::mbar_try_wait(a, 0) && tc::globaltimer_ns() - t0 < tc::kWaitLimitNs) {
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------------------------------------------------------- row statistics
+    const float al2 = alpha * kLog2e;
+    for (int i = 0; i < nQ; ++i) {
+      const int s = i & 1;
+      if (i >= 2 && !__all_sync(0xffffffffu, tc::mbar_wait(&bars->qd_empty[s], ((i >> 1) - 1) & 1,
+                                                            abort_flag, p.err, kErrTimeoutTma)))
+        break;
+      float* st = stats + s * 3 * kT;
+      for (int r = lane; r < kT; r += 32) {
+        const int q = i * kT + r;
+        float mc = 0.f, rz = 0.f, dq = 0.f;
+        if (q < p.Lq) {
+          const int64_t ri = bh * p.Lq + q;
+          mc = -p.row_max[ri] * al2;
+          rz = 1.f / p.row_z[ri];
+          dq = p.drow[ri];
+        }
+        st[r] = mc;
+        st[kT + r] = rz;
+        st[2 * kT + r] = dq;
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->qd_full[s]);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------------------------------------------------------- dQ epilogue
+    const int r = ((warp & 3) << 5) + lane;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) << 5) << 16;
+    float* stage = reinterpret_cast<float*>(smem + kOffStage);
+    bool ok = true;
+    for (int j = 0; j < nQ && ok; ++j) {
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->dq_full, j & 1, abort_flag, p.err, kErrTimeoutCompute));
+      if (!ok) break;
+      tc::tc_fence_after();
+      uint32_t a0[32], a1[32], a2[32];
+      tc::tmem_ld32(tmem + lane_base + kColDQ, a0);
+      tc::tmem_ld32(tmem + lane_base + kColDQ + 32, a1);
+      tc::tmem_ld32(tmem + lane_base + kColDQ + 64, a2);
+      tc::tmem_wait_ld();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->dq_free);
+      const int q = j * kT + r;
+      if (q < p.Lq) atomicAdd(p.ws_rowf + bh * p.Lq + q, __uint_as_float(a2[0]));
+      // the previous reduce must have finished reading the staging buffer
+      if (threadIdx.x == 128) tc::bulk_wait_group_read0();
+      tc::named_barrier_sync(1, 128);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int pc = (u ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(stage) + r * 128 + pc) =
+            make_uint4(a0[4 * u], a0[4 * u + 1], a0[4 * u + 2], a0[4 * u + 3]);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(stage) + kTile + r * 128 + pc) =
+            make_uint4(a1[4 * u], a1[4 * u + 1], a1[4 * u + 2], a1[4 * u + 3]);
+      }
+      tc::fence_async_smem();
+      tc::named_barrier_sync(1, 128);
+      if (threadIdx.x == 128) {
+        tc::tma_reduce_add_3d(&p.tdq, stage, 0, j * kT, static_cast<int>(bh));
+        tc::tma_reduce_add_3d(&p.tdq, reinterpret_cast<uint8_t*>(stage) + kTile, 32, j * kT,
+                              static_cast<int>(bh));
+        tc::bulk_commit_group();
+      }
+    }
+    // final dK / dV (one thread per key row)
+    if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->fin, 0, abort_flag, p.err, kErrTimeoutCompute));
+    if (ok) {
+      tc::tc_fence_after();
+      uint32_t v0[32], v1[32];
+      const int key = k0 + r;
+      tc::tmem_ld32(tmem + lane_base + kColDV, v0);
+      tc::tmem_ld32(tmem + lane_base + kColDV + 32, v1);
+      tc::tmem_wait_ld();
+      if (key < p.Lk) {
+        __nv_bfloat16* dvrow = static_cast<__nv_bfloat16*>(p.dv) + b * p.dvs[0] + h * p.dvs[1] +
+                               static_cast<int64_t>(key) * p.dvs[2];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 w;
+          w.x = tc::pack_bf16(__uint_as_float(v0[8 * u]), __uint_as_float(v0[8 * u + 1]));
+          w.y = tc::pack_bf16(__uint_as_float(v0[8 * u + 2]), __uint_as_float(v0[8 * u + 3]));
+          w.z = tc::pack_bf16(__uint_as_float(v0[8 * u + 4]), __uint_as_float(v0[8 * u + 5]));
+          w.w = tc::pack_bf16(__uint_as_float(v0[8 * u + 6]), __uint_as_float(v0[8 * u + 7]));
+          reinterpret_cast<uint4*>(dvrow)[u] = w;
+          w.x = tc::pack_bf16(__uint_as_float(v1[8 * u]), __uint_as_float(v1[8 * u + 1]));
+          w.y = tc::pack_bf16(__uint_as_float(v1[8 * u + 2]), __uint_as_float(v1[8 * u + 3]));
+          w.z = tc::pack_bf16(__uint_as_float(v1[8 * u + 4]), __uint_as_float(v1[8 * u + 5]));
+          w.w = tc::pack_bf16(__uint_as_float(v1[8 * u + 6]), __uint_as_float(v1[8 * u + 7]));
+          reinterpret_cast<uint4*>(dvrow)[4 + u] = w;
+        }
+      }
+      tc::tmem_ld32(tmem + lane_base + kColDK, v0);
+      tc::tmem_ld32(tmem + lane_base + kColDK + 32, v1);
+      tc::tmem_wait_ld();
+      if (key < p.Lk) {
+        float4* dkrow = reinterpret_cast<float4*>(p.ws_dk + (bh * p.Lk + key) * kD);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          dkrow[u] = make_float4(__uint_as_float(v0[4 * u]), __uint_as_float(v0[4 * u + 1]),
+                                 __uint_as_float(v0[4 * u + 2]), __uint_as_float(v0[4 * u + 3]));
+          dkrow[8 + u] = make_float4(__uint_as_float(v1[4 * u]), __uint_as_float(v1[4 * u + 1]),
+                                     __uint_as_float(v1[4 * u + 2]), __uint_as_float(v1[4 * u + 3]));
+        }
+      }
+    }
+    if (threadIdx.x == 128) tc::bulk_wait_group0();
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------------- elementwise
+    const int half = (warp - 8) >> 2;                // query columns [64 half, 64 half + 64)
+    const int r = ((warp & 3) << 5) + lane;          // key row = TMEM lane
+    const int key = k0 + r;
+    const bool key_ok = key < p.Lk;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) << 5) << 16;
+    const float al2 = alpha * kLog2e;
+    const float sa2 = p.scale * al2, inv_al2 = 1.f / al2, ta = tau * alpha;
+    const bool has_mask = p.mask != nullptr || p.causal;
+    uint8_t* Pt = smem + kOffP + half * kTile;
+    uint8_t* DSt = smem + kOffDS + half * kTile;
+    float acc_tau = 0.f, acc_alpha = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nQ && ok; ++i) {
+      const int s = i & 1;
+      ok = tc::mbar_wait(&bars->qd_full[s], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutCompute);
+      ok = ok && tc::mbar_wait(&bars->s_full, i & 1, abort_flag, p.err, kErrTimeoutCompute);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc::tc_fence_after();
+      const float* st = stats + s * 3 * kT;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = half * 64 + c * 32;
+        uint32_t sv[32], dv[32];
+        tc::tmem_ld32(tmem + lane_base + kColS + col0, sv);
+        tc::tmem_ld32(tmem + lane_base + kColDP + col0, dv);
+        tc::tmem_wait_ld();
+        if (c == 1) {
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bars->s_free);
+        }
+        uint32_t pp[16], pf[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float P2[2], F2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = col0 + e + u;
+            const float mc = st[col], rz = st[kT + col], dq = st[2 * kT + col];
+            float a2 = fmaf(__uint_as_float(sv[e + u]), sa2, mc);
+            if (has_mask) {
+              const int q = i * kT + col;
+              if (key_ok && q < p.Lq) a2 = fmaf(bwd_mask_value(p, b, h, q, key), al2, a2);
+            }
+            float lg, ratio;
+            sigma_terms<SIG>(a2, lg, ratio);
+            const float qv = fmaxf(tc::ex2(tau * lg), kClampMin);
+            const float P = key_ok ? qv * rz : 0.f;
+            const float t = P * (__uint_as_float(dv[e + u]) - dq);
+            const float g = fminf(fmaxf(ratio * (a2 * inv_al2), -30.f), 30.f);
+            acc_tau = fmaf(t, lg, acc_tau);
+            acc_alpha = fmaf(t, g, acc_alpha);
+            P2[u] = P;
+            F2[u] = ta * t * ratio;
+          }
+          pp[e >> 1] = tc::pack_bf16(P2[0], P2[1]);
+          pf[e >> 1] = tc::pack_bf16(F2[0], F2[1]);
+        }
+        if (c == 0 && i > 0) {
+          ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->p_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutCompute));
+          if (!ok) break;
+        }
+        // P^T / dS^T rows: key r, queries col0..col0+31 of the 64-query atom `half`
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int chunk = ((c * 4 + u) ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(Pt + r * 128 + chunk) =
+              make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
+          *reinterpret_cast<uint4*>(DSt + r * 128 + chunk) =
+              make_uint4(pf[4 * u], pf[4 * u + 1], pf[4 * u + 2], pf[4 * u + 3]);
+        }
+      }
+      if (!ok) break;
+      tc::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->ds_ready);
+    }
+    // per-head sums: dtau = ln2 * sum t * log2(sigma), dalpha = tau * sum t * g
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      acc_tau += __shfl_xor_sync(0xffffffffu, acc_tau, off);
+      acc_alpha += __shfl_xor_sync(0xffffffffu, acc_alpha, off);
+    }
+    if (lane == 0) {
+      atomicAdd(&bars->red_tau, acc_tau);
+      atomicAdd(&bars->red_alpha, acc_alpha);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && !*abort_flag) {
+    atomicAdd(p.dtau + h, bars->red_tau * kLn2);
+    atomicAdd(p.dalpha + h, bars->red_alpha * tau);
+  }
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+static bool layout16(const void* ptr, const int64_t s[4]) {
+  return s[3] == 1 && (reinterpret_cast<uintptr_t>(ptr) % 16 == 0) && s[0] % 8 == 0 &&
+         s[1] % 8 == 0 && s[2] % 8 == 0 && s[0] >= 0 && s[1] >= 0 && s[2] > 0;
+}
+
+bool attn_tensor_bwd_supported(const AttnProblem& p) {
+  if (!attn_tensor_supported(p)) return false;
+  return layout16(p.dout, p.dos) && layout16(p.dv, p.dvs);
+}
+
+int attn_bwd_tensor_main(const AttnProblem& p, cudaStream_t st) {
+  BwdParams bp;
+  memset(&bp, 0, sizeof(bp));
+  if (!make_tmap_bhld(&bp.tq, p.q, p.D, p.Lq, p.H, p.B, p.qs, kT) ||
+      !make_tmap_bhld(&bp.tk, p.k, p.D, p.Lk, p.H, p.B, p.ks, kT) ||
+      !make_tmap_bhld(&bp.tv, p.v, p.D, p.Lk, p.H, p.B, p.vs, kT) ||
+      !make_tmap_bhld(&bp.tdo, p.dout, p.D, p.Lq, p.H, p.B, p.dos, kT) ||
+      !make_tmap_f32_rows64(&bp.tdq, p.ws_dq, p.Lq, static_cast<int64_t>(p.B) * p.H, kT))
+    return TAU_DXB_ERR_CUDA;
+  bp.B = p.B; bp.H = p.H; bp.Lq = p.Lq; bp.Lk = p.Lk;
+  bp.tau = p.tau; bp.alpha = p.alpha; bp.scale = p.scale; bp.causal = p.causal;
+  bp.mask = p.mask; bp.mask_dtype = p.mask_dtype;
+  for (int i = 0; i < 4; ++i) { bp.ms[i] = p.ms[i]; bp.dvs[i] = p.dvs[i]; }
+  bp.row_max = p.row_max; bp.row_z = p.row_z; bp.drow = p.ws_drow;
+  bp.ws_rowf = p.ws_rowf; bp.ws_dk = p.ws_dk;
+  bp.dv = p.dv; bp.dtau = p.dtau; bp.dalpha = p.dalpha;
+  bp.err = device_error_word();
+  if (!bp.err) return fail(TAU_DXB_ERR_CUDA, "cannot resolve the device error word");
+  dim3 grid((p.Lk + kT - 1) / kT, p.H, p.B);
+  auto launch = [&](auto kern) -> int {
+    TDX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBwdSmem));
+    kern<<<grid, kThreads, kBwdSmem, st>>>(bp);
+    return check_launch("attn_bwd_tc_kernel");
+  };
+  switch (p.sigma) {
+    case TAU_DXB_SIGMA_SOFTPLUS: return launch(attn_bwd_tc_kernel<TAU_DXB_SIGMA_SOFTPLUS>);
+    case TAU_DXB_SIGMA_SIGMOID: return launch(attn_bwd_tc_kernel<TAU_DXB_SIGMA_SIGMOID>);
+    case TAU_DXB_SIGMA_EXP: return launch(attn_bwd_tc_kernel<TAU_DXB_SIGMA_EXP>);
+    default: return launch(attn_bwd_tc_kernel<TAU_DXB_SIGMA_RELU>);
+  }
+}
+
+}  // namespace taudxb

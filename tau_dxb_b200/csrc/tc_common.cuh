@@ -77,6 +77,28 @@ __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// shared -> global TMA reduce-add of a tiled fp32 box (bulk-group completion)
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1, int c2) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%1, %2, %3}], [%4];"
+      :: "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
 // ---- TMEM / tcgen05 ---------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -186,5 +208,9 @@ __device__ __forceinline__ float horner(const float (&c)[N], float x) {
 // 128-byte swizzle. Returns false (with a message) if the driver rejects it.
 bool make_tmap_bhld(CUtensorMap* map, const void* base, int64_t D, int64_t L, int64_t H, int64_t B,
                     const int64_t strides_elems[4], int box_rows);
+
+// host: 3-D fp32 tensor map over a contiguous [planes][rows][64] array with a
+// box of 32 x box_rows x 1 and 128-byte swizzle (the dQ accumulator).
+bool make_tmap_f32_rows64(CUtensorMap* map, void* base, int64_t rows, int64_t planes, int box_rows);
 
 }  // namespace taudxb
