@@ -147,6 +147,37 @@ TAU_DXB_API int tau_attn_bwd(const void* q, const int64_t q_stride[4],
                  int32_t path, void* stream);
 
 /*
+ * tau-opus attention backward that allocates nothing (no counterpart in the
+ * reference). For hosts that manage all device memory through their own pool
+ * or a fixed budget, and FFI callers without a device allocator: they cannot
+ * have the library call cudaMalloc (it bypasses their accounting and can
+ * synchronise the device) and may have no workspace to pass in.
+ * Same arguments and results as tau_attn_bwd without the workspace; the scratch
+ * lives in a fixed 16 MiB device array of the library (held on every GPU that
+ * loads the library until exit). Problems needing more than 16 MiB of
+ * workspace (tau_attn_bwd_workspace_bytes) return TAU_DXB_ERR_WORKSPACE. The
+ * first call on a device resolves the array's address there; make it before
+ * any stream capture. All calls on a device share the array: calls whose GPU
+ * work overlaps race and must be serialised by the caller.
+ */
+TAU_DXB_API int tau_attn_bwd_noalloc(const void* q, const int64_t q_stride[4],
+                 const void* k, const int64_t k_stride[4],
+                 const void* v, const int64_t v_stride[4],
+                 const void* out, const int64_t out_stride[4],
+                 const void* dout, const int64_t dout_stride[4],
+                 int32_t dtype, int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D,
+                 const float* tau, const float* alpha,
+                 int32_t sigma_id, float scale,
+                 const void* mask, int32_t mask_dtype, const int64_t mask_stride[4],
+                 int32_t causal,
+                 const float* row_max, const float* row_z, const int32_t* row_argmax,
+                 void* dq, const int64_t dq_stride[4],
+                 void* dk, const int64_t dk_stride[4],
+                 void* dv, const int64_t dv_stride[4],
+                 float* dtau, float* dalpha,
+                 int32_t path, void* stream);
+
+/*
  * WTA forward: per-row top-k selection over the last dimension.
  * Replaces _triton_wta_forward / _WTAFusedSTE.forward (echo/triton_wta.py:71-100),
  * _torch_wta_forward (echo/triton_wta.py:117-123) and the mask of

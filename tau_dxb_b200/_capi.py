@@ -56,6 +56,16 @@ SIGNATURES = {
         _vp, _vp,                                     # dtau, dalpha
         _vp, ctypes.c_size_t,                         # workspace
         _i32, _vp]),                                  # path, stream
+    "tau_attn_bwd_noalloc": (ctypes.c_int, [
+        _vp, _i64p, _vp, _i64p, _vp, _i64p,           # q, k, v
+        _vp, _i64p, _vp, _i64p,                       # out, dout
+        _i32, _i64, _i64, _i64, _i64, _i64,           # dtype, B, H, Lq, Lk, D
+        _vp, _vp, _i32, ctypes.c_float,               # tau, alpha, sigma, scale
+        _vp, _i32, _i64p, _i32,                       # mask
+        _vp, _vp, _vp,                                # row state
+        _vp, _i64p, _vp, _i64p, _vp, _i64p,           # dq, dk, dv
+        _vp, _vp,                                     # dtau, dalpha
+        _i32, _vp]),                                  # path, stream
     "wta_fwd": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _vp]),
     "wta_bwd": (ctypes.c_int, [_vp, _i32, _vp, _i64, _i64, _vp, _vp]),
     "wta_k_from_logits": (ctypes.c_int, [_vp, _i64, _i64, _vp, _vp]),
