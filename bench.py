@@ -267,6 +267,46 @@ def wta_sub_bench(torch, device, iters=20, warm=3):
     return res
 
 
+def train_sub_bench(torch, device, world, rank, steps=10, warmup=3):
+    """Whisper-small tau-opus + WTA train step (batch 16 per GPU, bf16 autocast,
+    fp32 master weights, AdamW); DDP + NCCL all-reduce when world > 1.
+    samples/s of the whole job, max-over-ranks CUDA-event time."""
+    import torch.distributed as dist
+    from tau_dxb_b200 import train as T
+    cfg = T.StepConfig(batch=16, seed=0)
+    step = T.TrainStep(cfg, device)
+    g = torch.Generator().manual_seed(10_000 + rank)
+    batches = [T.synthetic_batch(cfg, device, g) for _ in range(2)]
+    for i in range(warmup):
+        step.step(*batches[i % 2])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        step.step(*batches[i % 2])
+    e.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / steps], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    flops = T.model_flops_per_step(cfg)
+    peak = load_peaks()[2]
+    out = {"samples_per_s": round(world * cfg.batch / (ms * 1e-3), 2), "ms_per_step": round(ms, 2),
+           "n_gpus": world, "per_gpu_batch": cfg.batch, "global_batch": world * cfg.batch,
+           "model_tflop_per_step_per_gpu": round(flops / 1e12, 3),
+           "mfu_of_sustained_bf16": round(flops / (ms * 1e-3) / (peak * 1e12), 4),
+           "skipped_steps": step.skipped,
+           "parallelism": f"dp{world} (DDP, NCCL all-reduce of all gradients)" if world > 1 else "single GPU",
+           "data": "synthetic log-mel N(0,1) [16,80,3000], labels uniform over 51865, lengths U[64,448]"}
+    del step
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_baseline_sample(reps=1):
     """The oracle (numpy) on a bounded sample: B=1, H=12, L=1500 encoder fwd+bwd."""
     from oracle import stau_attention as OA
@@ -415,6 +455,11 @@ def run_ours(args, rank, world, local_rank):
         }
         if e2e:
             result["e2e"] = e2e
+    # the train step runs on every rank (DDP all-reduce when world > 1)
+    if not args.quick and not args.no_train:
+        ts = train_sub_bench(torch, device, world, rank)
+        if rank == 0:
+            result["train_step"] = ts
     # sub-benchmarks (rank 0 only, outside the timed region)
     if rank == 0 and not args.quick:
         subs = {}
@@ -480,6 +525,7 @@ def main():
     ap.add_argument("--long", action="store_true", help="add the L=6000 stress case")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-train", action="store_true", help="skip the Whisper train-step sub-benchmark")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (timing rule)")

@@ -1,0 +1,190 @@
+"""Attach learnable tau-opus attention to HuggingFace Whisper (B200 kernels).
+
+Same public functions as the reference module echo/patch_whisper_stau.py:
+  apply_learnable_stau(model, tau_init, alpha_init, sigma_name, default_tau_json,
+                       use_flash)                       (:325-405)
+  remove_stau(model)                                    (:408-415)
+  load_tau_dict(json_path)                              (:150-183)
+  STauOpusLearnable(n_heads, sigma_name)                (:115-133)
+  _classify_attn, _parse_layer_idx, _log_tau_for_init   (:140-147, :274-276, :267-271)
+
+Every WhisperAttention module gets a `_stau_opus` submodule owning per-head
+`log_tau` and `log_alpha` (state_dict keys `...self_attn._stau_opus.log_tau`
+as in the reference), and transformers' module-global
+`eager_attention_forward` is swapped for one that runs the fused operator.
+`use_flash` is accepted for signature compatibility; there is one operator.
+
+One addition: `assume_causal_decoder=True` tells the decoder self-attention
+sites that their additive mask is the plain causal mask (true in training
+with labels and no decoder padding mask); the kernels then apply causality
+from indices instead of reading the [B,1,L,L] mask tensor. Results are the
+same as with the mask tensor.
+"""
+from __future__ import annotations
+
+import json
+import math
+import re
+from pathlib import Path
+from typing import Dict, Union
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+from transformers.models.whisper import modeling_whisper as whisper_module
+
+from .attention import STauOpusAttentionFunction, STauOpusCausalFunction
+
+_ORIGINAL_EAGER_FORWARD = whisper_module.eager_attention_forward
+SITE_KINDS = ("encoder_self", "decoder_self", "decoder_cross")
+
+
+class STauOpusLearnable(nn.Module):
+    """tau-opus with learnable per-head tau = softplus(log_tau) + 1 and
+    alpha = exp(log_alpha) (echo/patch_whisper_stau.py:115-133)."""
+
+    def __init__(self, n_heads, sigma_name="softplus"):
+        super().__init__()
+        self.log_tau = nn.Parameter(torch.zeros(n_heads))
+        self.log_alpha = nn.Parameter(torch.zeros(n_heads))
+        self.sigma_name = sigma_name
+        self.assume_causal = False
+
+    def forward(self, Q, K, V, attn_mask=None, scale=None):
+        if self.assume_causal and attn_mask is not None and Q.shape[2] > 1:
+            return STauOpusCausalFunction.apply(Q, K, V, self.log_tau, self.log_alpha,
+                                                self.sigma_name, scale)
+        out, _ = STauOpusAttentionFunction.apply(Q, K, V, self.log_tau, self.log_alpha,
+                                                 self.sigma_name, attn_mask, scale)
+        return out
+
+
+def _classify_attn(name: str, module) -> str:
+    """encoder_self / decoder_self / decoder_cross (echo/patch_whisper_stau.py:140-147)."""
+    if not getattr(module, "is_decoder", False):
+        return "encoder_self"
+    if "encoder_attn" in name:
+        return "decoder_cross"
+    return "decoder_self"
+
+
+def _parse_layer_idx(name: str) -> int:
+    m = re.search(r"layers\.(\d+)", name)
+    return int(m.group(1)) if m else 0
+
+
+def load_tau_dict(json_path: Union[str, Path]) -> Dict[str, Dict[int, list]]:
+    """Read a tau* JSON (either record format of echo/patch_whisper_stau.py:150-183)
+    into {"encoder_self": {layer: [H taus]}, ...}."""
+    with open(json_path, "r", encoding="utf-8") as f:
+        data = json.load(f)
+    out = {k: {} for k in SITE_KINDS}
+    for item in data:
+        if "module_name" in item:
+            name = item["module_name"]
+            if "encoder_attn" in name:
+                key = "decoder_cross"
+            elif "decoder" in name and "self_attn" in name:
+                key = "decoder_self"
+            else:
+                key = "encoder_self"
+            layer = _parse_layer_idx(name)
+        else:
+            kind = item.get("attention_type")
+            if kind in out:
+                key = kind
+            elif item.get("cross_attention"):
+                key = "decoder_cross"
+            else:
+                key = "decoder_self" if item.get("is_decoder") else "encoder_self"
+            layer = item.get("layer_idx")
+            if layer is None:
+                layer = 0
+        out[key][layer] = item["tau_per_head"]
+    return out
+
+
+def _log_tau_for_init(tau: float) -> float:
+    """log_tau with softplus(log_tau) + 1 = tau; -8 for tau <= 1.001."""
+    if tau <= 1.001:
+        return -8.0
+    return math.log(math.exp(tau - 1.0) - 1.0)
+
+
+def _make_learnable_stau_forward():
+    def stau_eager_attention_forward(module, query, key, value, attention_mask, scaling=None,
+                                     dropout=0.0, **kwargs):
+        opus = getattr(module, "_stau_opus", None)
+        if opus is None:
+            raise RuntimeError("Module has no _stau_opus. Call apply_learnable_stau first.")
+        if scaling is None:
+            scaling = query.size(-1) ** -0.5
+        out = opus(query, key, value, attn_mask=attention_mask, scale=scaling)
+        out = F.dropout(out, p=dropout, training=module.training)
+        # the operator's output is a [B,H,L,D] view of a [B,L,H,D] buffer: no copy here
+        return out.transpose(1, 2).contiguous(), None
+    return stau_eager_attention_forward
+
+
+def _sigma_map(sigma_name):
+    if isinstance(sigma_name, str):
+        return {k: sigma_name for k in SITE_KINDS}
+    if isinstance(sigma_name, dict):
+        return {k: sigma_name.get(k, "softplus") for k in SITE_KINDS}
+    raise TypeError(f"Unsupported sigma_name type: {type(sigma_name)}")
+
+
+def apply_learnable_stau(model, tau_init=1.0, alpha_init: float = 1.0, sigma_name="softplus",
+                         default_tau_json=None, use_flash: bool = False,
+                         assume_causal_decoder: bool = False):
+    """Attach a learnable tau-opus operator to every WhisperAttention module."""
+    if isinstance(tau_init, (str, Path)):
+        if str(tau_init).lower() == "tau_star":
+            if default_tau_json is None:
+                raise ValueError("tau_init='tau_star' needs default_tau_json")
+            tau_dict = load_tau_dict(default_tau_json)
+        else:
+            tau_dict = load_tau_dict(tau_init)
+    elif isinstance(tau_init, dict):
+        tau_dict = tau_init
+    elif isinstance(tau_init, (float, int)):
+        tau_dict = None
+        scalar_tau = float(tau_init)
+    else:
+        raise TypeError(f"Unsupported tau_init type: {type(tau_init)}")
+    sigma_map = _sigma_map(sigma_name)
+
+    n_attached = 0
+    for name, module in model.named_modules():
+        if module.__class__.__name__ != "WhisperAttention":
+            continue
+        h = module.num_heads
+        kind = _classify_attn(name, module)
+        opus = STauOpusLearnable(h, sigma_name=sigma_map[kind]).to(next(module.parameters()).dtype)
+        opus = opus.to(next(module.parameters()).device)
+        opus.log_alpha.data.fill_(math.log(alpha_init))
+        if tau_dict is not None:
+            tau_list = tau_dict.get(kind, {}).get(_parse_layer_idx(name), [1.0] * h)
+        else:
+            tau_list = [scalar_tau] * h
+        tau_list = [max(1.0, float(t)) for t in tau_list[:h]]
+        opus.log_tau.data = torch.tensor([_log_tau_for_init(t) for t in tau_list],
+                                         dtype=opus.log_tau.dtype, device=opus.log_tau.device)
+        opus.assume_causal = bool(assume_causal_decoder and kind == "decoder_self")
+        module._stau_opus = opus
+        n_attached += 1
+    print(f"[tau-opus] Attached fused B200 STauOpus to {n_attached} attention modules")
+    print(f"  sigma config: {sigma_map}")
+    whisper_module.eager_attention_forward = _make_learnable_stau_forward()
+    return n_attached
+
+
+def remove_stau(model=None):
+    """Restore transformers' eager attention and clear the attached operators."""
+    whisper_module.eager_attention_forward = _ORIGINAL_EAGER_FORWARD
+    if model is not None:
+        for module in model.modules():
+            if module.__class__.__name__ == "WhisperAttention":
+                module._stau_tau = None
+                if "_stau_opus" in module._modules:
+                    del module._modules["_stau_opus"]

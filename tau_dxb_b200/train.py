@@ -1,0 +1,172 @@
+"""Whisper-small tau-opus + WTA fine-tune step, data-parallel over NCCL.
+
+One optimiser step of echo/train_echo_opus1.py:405-434 on B200:
+  bf16 autocast forward with fp32 master weights, loss = CE + lambda * mean
+  sigmoid(logit_k), backward through the fused tau-opus attention (36 sites)
+  and WTA / sparse_grad (24 FFNs), gradient all-reduce (NCCL, bucketed and
+  overlapped with the backward by DistributedDataParallel), clip_grad_norm 1.0,
+  AdamW with the reference's two parameter groups (base lr / tau lr for
+  log_tau and log_alpha, weight decay 0.01).
+
+Data parallelism shards by batch: every rank holds a replica and its own
+16-sample batch; the all-reduce averages every gradient, log_tau, log_alpha
+and logit_k included. A non-finite loss skips the step on every rank (the
+flag is all-reduced with the loss), as the reference skips NaN batches
+(echo/train_echo_opus1.py:422-425).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from . import patch_whisper_sparse_grad as SG
+from . import patch_whisper_stau as ST
+
+SIGMA_MAP = {"encoder_self": "softplus", "decoder_self": "sigmoid", "decoder_cross": "exp"}
+
+
+@dataclass
+class StepConfig:
+    batch: int = 16                 # per rank
+    n_mels: int = 80
+    frames: int = 3000
+    label_len: int = 448
+    min_label: int = 64
+    lr: float = 5e-6
+    tau_lr: float = 3e-4
+    weight_decay: float = 0.01
+    sparsity_lambda: float = 0.01
+    init_k_ratio: float = 0.4
+    clip: float = 1.0
+    encoder_layers: int = 12
+    decoder_layers: int = 12
+    d_model: int = 768
+    heads: int = 12
+    ffn: int = 3072
+    vocab: int = 51865
+    seed: int = 0
+    extra: dict = field(default_factory=dict)
+
+
+def whisper_config(cfg: StepConfig):
+    from transformers import WhisperConfig
+    special = {}
+    if cfg.vocab < 51865:   # reduced test vocabularies: keep the special tokens inside it
+        special = dict(pad_token_id=cfg.vocab - 1, bos_token_id=cfg.vocab - 2,
+                       eos_token_id=cfg.vocab - 1, decoder_start_token_id=cfg.vocab - 3)
+    c = WhisperConfig(vocab_size=cfg.vocab, d_model=cfg.d_model, encoder_layers=cfg.encoder_layers,
+                      decoder_layers=cfg.decoder_layers, encoder_attention_heads=cfg.heads,
+                      decoder_attention_heads=cfg.heads, encoder_ffn_dim=cfg.ffn,
+                      decoder_ffn_dim=cfg.ffn, max_source_positions=cfg.frames // 2,
+                      max_target_positions=cfg.label_len, num_mel_bins=cfg.n_mels, **special)
+    c._attn_implementation = "eager"
+    return c
+
+
+def synthetic_tau_init(cfg: StepConfig, seed: int = 1234):
+    """Seeded per-head tau initial values shaped like a tau* estimate: encoder
+    self-attention in [1.1, 1.9], decoder self-attention in [1.0, 4.6],
+    cross-attention 1.0."""
+    g = torch.Generator().manual_seed(seed)
+    out = {k: {} for k in ST.SITE_KINDS}
+    for layer in range(max(cfg.encoder_layers, cfg.decoder_layers)):
+        out["encoder_self"][layer] = (1.1 + 0.8 * torch.rand(cfg.heads, generator=g) ** 2).tolist()
+        out["decoder_self"][layer] = (1.0 + 3.6 * torch.rand(cfg.heads, generator=g) ** 3).tolist()
+        out["decoder_cross"][layer] = [1.0] * cfg.heads
+    return out
+
+
+def build_model(cfg: StepConfig, device, tau_init=None):
+    """Random-init Whisper with both patches applied (fp32 master weights)."""
+    from transformers import WhisperForConditionalGeneration
+    torch.manual_seed(cfg.seed)
+    model = WhisperForConditionalGeneration(whisper_config(cfg)).to(device)
+    ST.apply_learnable_stau(model, tau_init=tau_init if tau_init is not None else synthetic_tau_init(cfg),
+                            alpha_init=1.0, sigma_name=SIGMA_MAP, assume_causal_decoder=True)
+    SG.apply_sparse_grad_wta(model, target="encoder+decoder", encoder_mode="wta_activation",
+                             decoder_mode="sparse_grad", learnable_k=True,
+                             init_k_ratio=cfg.init_k_ratio, track_wins=True)
+    model.train()
+    return model
+
+
+def make_optimizer(model, cfg: StepConfig):
+    """AdamW with the reference's groups (echo/train_echo_opus1.py:344-355)."""
+    base, taup = [], []
+    for name, p in model.named_parameters():
+        if not p.requires_grad:
+            continue
+        (taup if ("log_tau" in name or "log_alpha" in name) else base).append(p)
+    fused = all(p.is_cuda for p in base + taup)
+    return torch.optim.AdamW([{"params": base, "lr": cfg.lr}, {"params": taup, "lr": cfg.tau_lr}],
+                             weight_decay=cfg.weight_decay, fused=fused)
+
+
+def synthetic_batch(cfg: StepConfig, device, generator: torch.Generator):
+    """log-mel [B, 80, 3000] ~ N(0,1); labels uniform over the vocabulary with
+    lengths uniform in [64, 448], padded with -100 to 448."""
+    mel = torch.randn(cfg.batch, cfg.n_mels, cfg.frames, generator=generator)
+    labels = torch.randint(0, cfg.vocab, (cfg.batch, cfg.label_len), generator=generator)
+    lens = torch.randint(cfg.min_label, cfg.label_len + 1, (cfg.batch,), generator=generator)
+    labels[torch.arange(cfg.label_len)[None, :] >= lens[:, None]] = -100
+    return mel.to(device, non_blocking=True), labels.to(device, non_blocking=True)
+
+
+class TrainStep:
+    """One fine-tune step on this rank (DDP-wrapped when a process group exists)."""
+
+    def __init__(self, cfg: StepConfig, device, tau_init=None, bucket_mb: int = 64):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.model = build_model(cfg, self.device, tau_init)
+        self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+        self.net = self.model
+        if self.world > 1:
+            from torch.nn.parallel import DistributedDataParallel as DDP
+            self.net = DDP(self.model, device_ids=[self.device.index] if self.device.type == "cuda" else None,
+                           bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True,
+                           broadcast_buffers=False)
+        self.opt = make_optimizer(self.model, cfg)
+        self.skipped = 0
+
+    def loss(self, mel, labels):
+        amp = torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.device.type == "cuda")
+        with amp:
+            ce = self.net(input_features=mel, labels=labels).loss
+            sp = SG.get_sparsity_loss().to(ce.device)
+            return ce + self.cfg.sparsity_lambda * sp, ce
+
+    def step(self, mel, labels):
+        """Forward, backward (+ all-reduce), clip, AdamW. Returns the loss tensor."""
+        loss, ce = self.loss(mel, labels)
+        loss.backward()
+        bad = (~torch.isfinite(loss.detach())).float().reshape(1)
+        if self.world > 1:
+            dist.all_reduce(bad)
+        if float(bad.item()) > 0:       # every rank skips together
+            self.opt.zero_grad(set_to_none=True)
+            self.skipped += 1
+            return loss.detach()
+        torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.clip)
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=True)
+        return loss.detach()
+
+
+def model_flops_per_step(cfg: StepConfig) -> float:
+    """Algorithmic FLOPs of one step (6 * weights * tokens for the linears, the
+    conv stem, and 3.5x the forward attention-score work)."""
+    d, f, T_enc, T_dec, B = cfg.d_model, cfg.ffn, cfg.frames // 2, cfg.label_len, cfg.batch
+    enc_lin = cfg.encoder_layers * (4 * d * d + 2 * d * f)
+    dec_self = cfg.decoder_layers * (4 * d * d + 2 * d * f)
+    dec_cross_qo = cfg.decoder_layers * 2 * d * d
+    dec_cross_kv = cfg.decoder_layers * 2 * d * d
+    head = cfg.vocab * d
+    lin = 6 * B * (enc_lin * T_enc + (dec_self + dec_cross_qo + head) * T_dec + dec_cross_kv * T_enc)
+    conv = 6 * B * (cfg.n_mels * d * 3 * cfg.frames + d * d * 3 * T_enc)
+    attn = 3.5 * 4 * B * cfg.heads * 64 * (
+        cfg.encoder_layers * T_enc * T_enc + cfg.decoder_layers * (0.5 * T_dec * T_dec + T_dec * T_enc))
+    return float(lin + conv + attn)
