@@ -274,7 +274,9 @@ def train_sub_bench(torch, device, world, rank, steps=10, warmup=3):
     import torch.distributed as dist
     from tau_dxb_b200 import train as T
     cfg = T.StepConfig(batch=16, seed=0)
-    step = T.TrainStep(cfg, device)
+    import contextlib
+    with contextlib.redirect_stdout(sys.stderr):     # stdout carries only the JSON line
+        step = T.TrainStep(cfg, device)
     g = torch.Generator().manual_seed(10_000 + rank)
     batches = [T.synthetic_batch(cfg, device, g) for _ in range(2)]
     for i in range(warmup):

@@ -32,6 +32,9 @@ def _run(cfg, device, mel, labels):
 
 def test_fp32_step_matches_oracle_model(monkeypatch):
     from tau_dxb_b200 import train as T
+    # full fp32 everywhere else in the model (cuDNN convolutions default to TF32)
+    monkeypatch.setattr(torch.backends.cudnn, "allow_tf32", False)
+    monkeypatch.setattr(torch.backends.cuda.matmul, "allow_tf32", False)
     cfg = tiny_cfg()
     mel, labels = T.synthetic_batch(cfg, "cpu", torch.Generator().manual_seed(7))
     with monkeypatch.context() as m:
