@@ -19,7 +19,10 @@
 //
 // Per score element the forward spends two special-function ops (exp2) for
 // softplus/sigmoid and one for exp: log2 sigma(x) is evaluated as
-// x log2(e) + G(exp(x)) with G a polynomial on [0, 1] (poly_coeffs.h).
+// x log2(e) + G(exp(x)) with G a polynomial on [0, 1] (poly_coeffs.h), tau
+// is folded into the polynomial's coefficients and the two clamps of the
+// reference collapse into one. TMEM loads are double-buffered: the next
+// 32-column chunk is in flight while the current one is processed.
 
 #include "attn.h"
 #include "poly_coeffs.h"
@@ -105,24 +108,6 @@ constexpr uint32_t kSmemP = kSmemV + kStages * kTileBytes;       // 2 x 32 KB
 constexpr uint32_t kSmemBar = kSmemP + 2 * 2 * kTileBytes;
 constexpr uint32_t kFwdSmemBytes = kSmemBar + sizeof(FwdBarriers) + 1024;  // + alignment slack
 
-// log2(sigma(x)) for x <= 0, given a2 = x * log2(e); clamped at log2(1e-8)
-template <int SIG>
-__device__ __forceinline__ float log2_sigma(float a2) {
-  float lg;
-  if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
-    const float e = tc::ex2(a2);
-    lg = a2 + poly::G(e);
-  } else if (SIG == TAU_DXB_SIGMA_SIGMOID) {
-    const float e = tc::ex2(a2);
-    lg = a2 - poly::H(e);
-  } else if (SIG == TAU_DXB_SIGMA_EXP) {
-    lg = a2;
-  } else {
-    lg = kLog2Clamp;   // relu(x <= 0) = 0, clamped to 1e-8
-  }
-  return fmaxf(lg, kLog2Clamp);
-}
-
 __device__ __forceinline__ float fwd_mask_value(const FwdParams& p, int b, int h, int r, int c) {
   float mv = 0.f;
   if (p.mask) {
@@ -137,7 +122,9 @@ __device__ __forceinline__ float fwd_mask_value(const FwdParams& p, int b, int h
 template <int SIG>
 __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base by pointer arithmetic on the __shared__ array, so the
+  // compiler keeps every derived pointer in the shared address space
+  uint8_t* smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(smem + kSmemBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * 2 * kBM;
@@ -294,90 +281,138 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
     int i = 0;
     float m = -INFINITY;
     int amax = 0;
-    // pass 1: exact row max and first argmax
+    // pass 1: exact row max and first argmax (scores in increasing key order;
+    // a later chunk replaces the running max only if strictly larger)
+    auto pass1_chunk = [&](const uint32_t (&v)[32], int key0, bool fast) {
+      if (fast) {
+        float cm = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) cm = fmaxf(cm, __uint_as_float(v[e]) * p.scale);
+        if (cm > m) {
+          int first = 0;
+#pragma unroll
+          for (int e = 31; e >= 0; --e)
+            if (__uint_as_float(v[e]) * p.scale == cm) first = e;
+          m = cm;
+          amax = key0 + first;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int key = key0 + e;
+          if (key < p.Lk) {
+            float sv = __uint_as_float(v[e]) * p.scale;
+            if (has_mask && row_ok) sv += fwd_mask_value(p, b, h, grow, key);
+            if (sv > m) { m = sv; amax = key; }
+          }
+        }
+      }
+    };
     for (int j = 0; j < nK && ok; ++j, ++i) {
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->s_full[t], i & 1, abort_flag, p.err, kErrTimeoutSoftmax));
       if (!ok) break;
       tc::tc_fence_after();
+      const bool fast = (j + 1) * kBN <= p.Lk && !has_mask;
+      uint32_t va[32], vb[32];
+      tc::tmem_ld32(tS, va);
+      tc::tmem_wait_ld_regs(va);
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t v[32];
-        tc::tmem_ld32(tS + c * 32, v);
-        tc::tmem_wait_ld();
-        const int key0 = j * kBN + c * 32;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = key0 + e;
-          float sv = __uint_as_float(v[e]) * p.scale;
-          if (has_mask && row_ok && key < p.Lk) sv += fwd_mask_value(p, b, h, grow, key);
-          if (key < p.Lk && sv > m) { m = sv; amax = key; }
-        }
+      for (int c = 0; c < kBN / 32; c += 2) {
+        tc::tmem_ld32(tS + (c + 1) * 32, vb);           // next chunk in flight
+        pass1_chunk(va, j * kBN + c * 32, fast);
+        tc::tmem_wait_ld_regs(vb);
+        if (c + 2 < kBN / 32) tc::tmem_ld32(tS + (c + 2) * 32, va);
+        pass1_chunk(vb, j * kBN + (c + 1) * 32, fast);
+        if (c + 2 < kBN / 32) tc::tmem_wait_ld_regs(va);
       }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->sp_ready[t]);
     }
     if (!row_ok) m = 0.f;
-    // pass 2: q = max(sigma(alpha (s - m))^tau, 1e-8)
+    // pass 2: q = max(sigma(alpha (s - m))^tau, 1e-8) = 2^max(tau log2 sigma, ylo)
+    // with ylo = max(tau, 1) * log2(1e-8), the two clamps of the reference folded
+    // into one (tau log2 sigma_clamped >= tau log2(1e-8)).
     const float al2 = alpha * kLog2e;
     const float sa2 = p.scale * al2, ma2 = m * al2;
-    float l = 0.f;
+    const float ylo = fmaxf(tau * kLog2Clamp, kLog2Clamp);
+    float l0 = 0.f, l1 = 0.f;
+    auto qval = [&](float a2) -> float {
+      float y;
+      if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
+        y = fmaf(tau, a2, poly::G_scaled(tc::ex2(a2), tau));
+      } else if (SIG == TAU_DXB_SIGMA_SIGMOID) {
+        y = fmaf(tau, a2, -poly::H_scaled(tc::ex2(a2), tau));
+      } else if (SIG == TAU_DXB_SIGMA_EXP) {
+        y = tau * a2;
+      } else {
+        y = ylo;   // relu(x <= 0) = 0 -> clamped sigma 1e-8
+      }
+      return tc::ex2(fmaxf(y, ylo));
+    };
+    auto pass2_chunk = [&](const uint32_t (&v)[32], int c, int key0, bool full) {
+      uint32_t pk[16];
+      if (full) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float q0v = qval(fmaf(__uint_as_float(v[e]), sa2, -ma2));
+          const float q1v = qval(fmaf(__uint_as_float(v[e + 1]), sa2, -ma2));
+          l0 += q0v;
+          l1 += q1v;
+          pk[e >> 1] = tc::pack_bf16(q0v, q1v);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float qq[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int key = key0 + e + u;
+            float qv = 0.f;
+            if (key < p.Lk) {
+              float sv = __uint_as_float(v[e + u]) * p.scale;
+              if (has_mask && row_ok) sv += fwd_mask_value(p, b, h, grow, key);
+              qv = qval((sv - m) * al2);
+            }
+            qq[u] = qv;
+          }
+          l0 += qq[0];
+          l1 += qq[1];
+          pk[e >> 1] = tc::pack_bf16(qq[0], qq[1]);
+        }
+      }
+      // 32 keys -> 4 x 16-byte chunks of the 128B-swizzled K-major P tile
+      uint8_t* rowp = Pt + (c >> 1) * kTileBytes + r * 128;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int chunk = ((c & 1) * 4 + u) ^ (r & 7);
+        *reinterpret_cast<uint4*>(rowp + chunk * 16) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      }
+    };
     for (int j = 0; j < nK && ok; ++j, ++i) {
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->s_full[t], i & 1, abort_flag, p.err, kErrTimeoutSoftmax));
       if (!ok) break;
       tc::tc_fence_after();
       const bool full = (j + 1) * kBN <= p.Lk && !has_mask;
+      uint32_t va[32], vb[32];
+      tc::tmem_ld32(tS, va);
+      tc::tmem_wait_ld_regs(va);
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t v[32];
-        tc::tmem_ld32(tS + c * 32, v);
-        tc::tmem_wait_ld();
-        uint32_t pk[16];
-        const int key0 = j * kBN + c * 32;
-        if (full) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float a0 = fmaf(__uint_as_float(v[e]), sa2, -ma2);
-            const float a1 = fmaf(__uint_as_float(v[e + 1]), sa2, -ma2);
-            const float q0v = fmaxf(tc::ex2(tau * log2_sigma<SIG>(a0)), kClampMin);
-            const float q1v = fmaxf(tc::ex2(tau * log2_sigma<SIG>(a1)), kClampMin);
-            l += q0v + q1v;
-            pk[e >> 1] = tc::pack_bf16(q0v, q1v);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float qq[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int key = key0 + e + u;
-              float qv = 0.f;
-              if (key < p.Lk) {
-                float sv = __uint_as_float(v[e + u]) * p.scale;
-                if (has_mask && row_ok) sv += fwd_mask_value(p, b, h, grow, key);
-                const float a2 = (sv - m) * al2;
-                qv = fmaxf(tc::ex2(tau * log2_sigma<SIG>(a2)), kClampMin);
-              }
-              qq[u] = qv;
-              l += qv;
-            }
-            pk[e >> 1] = tc::pack_bf16(qq[0], qq[1]);
-          }
-        }
-        // 32 keys -> 4 x 16-byte chunks of the 128B-swizzled K-major P tile
-        uint8_t* rowp = Pt + (c >> 1) * kTileBytes + r * 128;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int chunk = ((c & 1) * 4 + u) ^ (r & 7);
-          *reinterpret_cast<uint4*>(rowp + chunk * 16) =
-              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-        }
+      for (int c = 0; c < kBN / 32; c += 2) {
+        tc::tmem_ld32(tS + (c + 1) * 32, vb);           // next chunk in flight
+        pass2_chunk(va, c, j * kBN + c * 32, full);
+        tc::tmem_wait_ld_regs(vb);
+        if (c + 2 < kBN / 32) tc::tmem_ld32(tS + (c + 2) * 32, va);
+        pass2_chunk(vb, c + 1, j * kBN + (c + 1) * 32, full);
+        if (c + 2 < kBN / 32) tc::tmem_wait_ld_regs(va);
       }
       tc::fence_async_smem();
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->sp_ready[t]);
     }
+    const float l = l0 + l1;
     // epilogue: O / Z
     if (ok) ok = tc::mbar_wait(&bars->o_full[t], 0, abort_flag, p.err, kErrTimeoutSoftmax);
     ok = __all_sync(0xffffffffu, ok);

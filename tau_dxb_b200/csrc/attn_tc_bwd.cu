@@ -114,27 +114,6 @@ constexpr uint32_t kBwdSmem = kOffBar + sizeof(BwdBarriers) + 1024;
 
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
 
-// log2 sigma and sigma'/sigma for x <= 0 from a2 = x log2(e)
-template <int SIG>
-__device__ __forceinline__ void sigma_terms(float a2, float& lg, float& ratio) {
-  if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
-    const float e = tc::ex2(a2);
-    lg = a2 + poly::G(e);
-    ratio = poly::R(e);
-  } else if (SIG == TAU_DXB_SIGMA_SIGMOID) {
-    const float e = tc::ex2(a2);
-    lg = a2 - poly::H(e);
-    ratio = poly::S(e);
-  } else if (SIG == TAU_DXB_SIGMA_EXP) {
-    lg = a2;
-    ratio = 1.f;
-  } else {
-    lg = kLog2Clamp;
-    ratio = 1.f;
-  }
-  lg = fmaxf(lg, kLog2Clamp);
-}
-
 __device__ __forceinline__ float bwd_mask_value(const BwdParams& p, int b, int h, int r, int c) {
   float mv = 0.f;
   if (p.mask) {
@@ -149,7 +128,9 @@ __device__ __forceinline__ float bwd_mask_value(const BwdParams& p, int b, int h
 template <int SIG>
 __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_constant__ BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base by pointer arithmetic on the __shared__ array, so the
+  // compiler keeps every derived pointer in the shared address space
+  uint8_t* smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
   BwdBarriers* bars = reinterpret_cast<BwdBarriers*>(smem + kOffBar);
   float* stats = reinterpret_cast<float*>(smem + kOffStats);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -292,18 +273,23 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
                                                             abort_flag, p.err, kErrTimeoutTma)))
         break;
       float* st = stats + s * 3 * kT;
-      for (int r = lane; r < kT; r += 32) {
-        const int q = i * kT + r;
-        float mc = 0.f, rz = 0.f, dq = 0.f;
-        if (q < p.Lq) {
-          const int64_t ri = bh * p.Lq + q;
-          mc = -p.row_max[ri] * al2;
-          rz = 1.f / p.row_z[ri];
-          dq = p.drow[ri];
-        }
-        st[r] = mc;
-        st[kT + r] = rz;
-        st[2 * kT + r] = dq;
+      // all 12 loads of this lane in flight at once (one round of global latency)
+      float m4[4], z4[4], d4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int q = i * kT + lane + 32 * u;
+        const int64_t ri = bh * p.Lq + (q < p.Lq ? q : 0);
+        m4[u] = p.row_max[ri];
+        z4[u] = p.row_z[ri];
+        d4[u] = p.drow[ri];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int r = lane + 32 * u;
+        const bool q_ok = i * kT + r < p.Lq;
+        st[r] = q_ok ? -m4[u] * al2 : 0.f;
+        st[kT + r] = q_ok ? 1.f / z4[u] : 0.f;
+        st[2 * kT + r] = q_ok ? d4[u] : 0.f;
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->qd_full[s]);
@@ -392,18 +378,89 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     if (threadIdx.x == 128) tc::bulk_wait_group0();
   } else if (warp >= 8) {
     // ---------------------------------------------------------------- elementwise
+    // Per score: a2 = log2(e) alpha (s scale - m), y = tau log2 sigma (tau folded
+    // into the polynomial), q = 2^max(y, ylo) (both clamps of the reference in
+    // one), P = q / Z, t = P (dP - D), F = tau alpha t sigma'/sigma.
+    // Sums kept scaled: acc_tau = sum t tau log2 sigma_clamped and
+    // acc_alpha = sum t clip(ratio a2, +-30 log2(e) alpha); the constants are
+    // divided out once per CTA.
     const int half = (warp - 8) >> 2;                // query columns [64 half, 64 half + 64)
     const int r = ((warp & 3) << 5) + lane;          // key row = TMEM lane
     const int key = k0 + r;
     const bool key_ok = key < p.Lk;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) << 5) << 16;
     const float al2 = alpha * kLog2e;
-    const float sa2 = p.scale * al2, inv_al2 = 1.f / al2, ta = tau * alpha;
+    const float sa2 = p.scale * al2, ta = tau * alpha;
+    const float ylo = fmaxf(tau * kLog2Clamp, kLog2Clamp);
+    const float ytau = tau * kLog2Clamp;
+    const float glim = 30.f * al2;
+    const float kmask = key_ok ? 1.f : 0.f;
     const bool has_mask = p.mask != nullptr || p.causal;
     uint8_t* Pt = smem + kOffP + half * kTile;
     uint8_t* DSt = smem + kOffDS + half * kTile;
     float acc_tau = 0.f, acc_alpha = 0.f;
     bool ok = true;
+    // 16 query columns: scores sv, dP dv -> packed bf16 P (pp) and F (pf)
+    auto chunk16 = [&](const uint32_t* sv, const uint32_t* dv, const float* st, int col0, int i,
+                       uint32_t* pp, uint32_t* pf) {
+#pragma unroll
+      for (int e4 = 0; e4 < 16; e4 += 4) {
+        const float4 mc4 = *reinterpret_cast<const float4*>(st + col0 + e4);
+        const float4 rz4 = *reinterpret_cast<const float4*>(st + kT + col0 + e4);
+        const float4 dq4 = *reinterpret_cast<const float4*>(st + 2 * kT + col0 + e4);
+        const float mc[4] = {mc4.x, mc4.y, mc4.z, mc4.w};
+        const float rz[4] = {rz4.x, rz4.y, rz4.z, rz4.w};
+        const float dq[4] = {dq4.x, dq4.y, dq4.z, dq4.w};
+        float P4[4], F4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = e4 + u;
+          float a2 = fmaf(__uint_as_float(sv[e]), sa2, mc[u]);
+          if (has_mask) {
+            const int q = i * kT + col0 + e;
+            if (key_ok && q < p.Lq) a2 = fmaf(bwd_mask_value(p, b, h, q, key), al2, a2);
+          }
+          float y, ratio;
+          if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
+            const float ex = tc::ex2(a2);
+            y = fmaf(tau, a2, poly::G_scaled(ex, tau));
+            ratio = poly::R(ex);
+          } else if (SIG == TAU_DXB_SIGMA_SIGMOID) {
+            const float ex = tc::ex2(a2);
+            y = fmaf(tau, a2, -poly::H_scaled(ex, tau));
+            ratio = poly::S(ex);
+          } else if (SIG == TAU_DXB_SIGMA_EXP) {
+            y = tau * a2;
+            ratio = 1.f;
+          } else {
+            y = ytau;
+            ratio = 1.f;
+          }
+          const float qv = tc::ex2(fmaxf(y, ylo));
+          const float P = qv * rz[u] * kmask;
+          const float t = P * (__uint_as_float(dv[e]) - dq[u]);
+          acc_tau = fmaf(t, fmaxf(y, ytau), acc_tau);
+          acc_alpha = fmaf(t, fminf(fmaxf(ratio * a2, -glim), glim), acc_alpha);
+          P4[u] = P;
+          F4[u] = ta * (t * ratio);
+        }
+        pp[e4 >> 1] = tc::pack_bf16(P4[0], P4[1]);
+        pp[(e4 >> 1) + 1] = tc::pack_bf16(P4[2], P4[3]);
+        pf[e4 >> 1] = tc::pack_bf16(F4[0], F4[1]);
+        pf[(e4 >> 1) + 1] = tc::pack_bf16(F4[2], F4[3]);
+      }
+    };
+    // P^T / dS^T rows: key r, 16 queries = two 16-byte chunks of the 64-query atom
+    auto store16 = [&](int c, const uint32_t* pp, const uint32_t* pf) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int chunk = ((c * 2 + u) ^ (r & 7)) << 4;
+        *reinterpret_cast<uint4*>(Pt + r * 128 + chunk) =
+            make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
+        *reinterpret_cast<uint4*>(DSt + r * 128 + chunk) =
+            make_uint4(pf[4 * u], pf[4 * u + 1], pf[4 * u + 2], pf[4 * u + 3]);
+      }
+    };
     for (int i = 0; i < nQ && ok; ++i) {
       const int s = i & 1;
       ok = tc::mbar_wait(&bars->qd_full[s], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutCompute);
@@ -412,65 +469,42 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       if (!ok) break;
       tc::tc_fence_after();
       const float* st = stats + s * 3 * kT;
+      const uint32_t tS = tmem + lane_base + kColS + half * 64;
+      const uint32_t tP = tmem + lane_base + kColDP + half * 64;
+      uint32_t ra[32], rb[32];     // [0,16) scores, [16,32) dP of one 16-column chunk
+      tc::tmem_ld16(tS, ra);
+      tc::tmem_ld16(tP, ra + 16);
+      tc::tmem_wait_ld_regs(ra);
+      bool pfree_ok = true;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        const int col0 = half * 64 + c * 32;
-        uint32_t sv[32], dv[32];
-        tc::tmem_ld32(tmem + lane_base + kColS + col0, sv);
-        tc::tmem_ld32(tmem + lane_base + kColDP + col0, dv);
-        tc::tmem_wait_ld();
-        if (c == 1) {
+      for (int c = 0; c < 4; c += 2) {
+        tc::tmem_ld16(tS + (c + 1) * 16, rb);                 // next chunk in flight
+        tc::tmem_ld16(tP + (c + 1) * 16, rb + 16);
+        uint32_t pp[8], pf[8];
+        chunk16(ra, ra + 16, st, half * 64 + c * 16, i, pp, pf);
+        if (c == 0 && i > 0)   // the previous tile's MMAs must be done with P^T / dS^T
+          pfree_ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->p_free, (i - 1) & 1, abort_flag,
+                                                          p.err, kErrTimeoutCompute));
+        if (pfree_ok) store16(c, pp, pf);
+        tc::tmem_wait_ld_regs(rb);
+        if (c + 2 < 4) {
+          tc::tmem_ld16(tS + (c + 2) * 16, ra);
+          tc::tmem_ld16(tP + (c + 2) * 16, ra + 16);
+        } else {        // every TMEM read of this tile is done
           tc::tc_fence_before();
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(&bars->s_free);
         }
-        uint32_t pp[16], pf[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float P2[2], F2[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = col0 + e + u;
-            const float mc = st[col], rz = st[kT + col], dq = st[2 * kT + col];
-            float a2 = fmaf(__uint_as_float(sv[e + u]), sa2, mc);
-            if (has_mask) {
-              const int q = i * kT + col;
-              if (key_ok && q < p.Lq) a2 = fmaf(bwd_mask_value(p, b, h, q, key), al2, a2);
-            }
-            float lg, ratio;
-            sigma_terms<SIG>(a2, lg, ratio);
-            const float qv = fmaxf(tc::ex2(tau * lg), kClampMin);
-            const float P = key_ok ? qv * rz : 0.f;
-            const float t = P * (__uint_as_float(dv[e + u]) - dq);
-            const float g = fminf(fmaxf(ratio * (a2 * inv_al2), -30.f), 30.f);
-            acc_tau = fmaf(t, lg, acc_tau);
-            acc_alpha = fmaf(t, g, acc_alpha);
-            P2[u] = P;
-            F2[u] = ta * t * ratio;
-          }
-          pp[e >> 1] = tc::pack_bf16(P2[0], P2[1]);
-          pf[e >> 1] = tc::pack_bf16(F2[0], F2[1]);
-        }
-        if (c == 0 && i > 0) {
-          ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->p_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutCompute));
-          if (!ok) break;
-        }
-        // P^T / dS^T rows: key r, queries col0..col0+31 of the 64-query atom `half`
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int chunk = ((c * 4 + u) ^ (r & 7)) << 4;
-          *reinterpret_cast<uint4*>(Pt + r * 128 + chunk) =
-              make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
-          *reinterpret_cast<uint4*>(DSt + r * 128 + chunk) =
-              make_uint4(pf[4 * u], pf[4 * u + 1], pf[4 * u + 2], pf[4 * u + 3]);
-        }
+        chunk16(rb, rb + 16, st, half * 64 + (c + 1) * 16, i, pp, pf);
+        if (pfree_ok) store16(c + 1, pp, pf);
+        if (c + 2 < 4) tc::tmem_wait_ld_regs(ra);
       }
+      ok = pfree_ok;
       if (!ok) break;
       tc::fence_async_smem();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->ds_ready);
     }
-    // per-head sums: dtau = ln2 * sum t * log2(sigma), dalpha = tau * sum t * g
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       acc_tau += __shfl_xor_sync(0xffffffffu, acc_tau, off);
@@ -484,8 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
   tc::tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && !*abort_flag) {
-    atomicAdd(p.dtau + h, bars->red_tau * kLn2);
-    atomicAdd(p.dalpha + h, bars->red_alpha * tau);
+    // dtau = sum t ln(sigma_clamped), dalpha = tau sum t clip(sigma'/sigma (s - m), +-30)
+    atomicAdd(p.dtau + h, bars->red_tau * (kLn2 / tau));
+    atomicAdd(p.dalpha + h, bars->red_alpha * (tau / (alpha * kLog2e)));
   }
   if (warp == 1) {
     tc::tc_fence_after();

@@ -7,7 +7,7 @@
 #include <stdint.h>
 #include <stddef.h>
 
-#include "../../include/tau_dxb.h"
+#include "tau_dxb.h"
 
 namespace taudxb {
 
