@@ -6,20 +6,18 @@
 //   dP^T = V dO_i^T         (M=128,      N=128,         K=64)   -> TMEM [128,256)
 //   elementwise, one thread per key row: P = q / Z and
 //     F = tau alpha P (dP - D) sigma'/sigma   (the reference's d_s_stable before
-//     the argmax shift, echo/stau_opus_operator.py:134-137), written as bf16
-//     P^T and dS^T = F^T tiles in 128B-swizzled shared memory;
-//     dtau / dalpha partial sums stay in registers.
-//   dV  += P^T dO_i         (M=128 keys, N=64, K=128 queries)   -> TMEM [256,320)
-//   dK  += dS^T Q_i                                              -> TMEM [320,384)
-//   dQ_i = dS [K | 1]       (M=128 queries, N=80, K=128 keys)   -> TMEM [384,464)
-//     The dS^T buffer doubles as the MN-major A operand of this MMA, and the
-//     extra all-ones column of B yields rowsum_keys(F) in column 64 -- the
-//     quantity the argmax correction needs.
-//   dQ_i leaves through a TMA bulk reduce-add into the fp32 dQ accumulator;
-//   its rowsum column is added to the rowsum(F) accumulator.
-// Warp roles (16 warps): 0 TMA, 1 MMA + TMEM owner, 2 row statistics of each
-// query tile, 4-7 dQ epilogue (and the final dK / dV store), 8-15 elementwise
-// (two groups of 4 warps, query columns [0,64) and [64,128)).
+//     the argmax shift, echo/stau_opus_operator.py:134-137); P^T goes to TMEM
+//     [448,512) as packed bf16, dS^T = F^T / (tau alpha) to a double-buffered
+//     128B-swizzled shared-memory tile; dtau / dalpha stay in registers.
+//     The per-head factor tau alpha is applied once, to dQ, dK and rowsum(F),
+//     by the epilogue warps, which also reduce rowsum_keys(F) from the dS^T tile.
+//   dV  += P^T dO_i         (M=128 keys, N=64, K=128 queries; A from TMEM) -> [256,320)
+//   dK  += dS^T Q_i         (A = dS^T K-major in shared memory)            -> [320,384)
+//   dQ_i = dS K             (M=128 queries; the same dS^T tile as MN-major A) -> [384,448)
+//   dQ_i leaves through a TMA bulk reduce-add into the fp32 dQ accumulator.
+// Warp roles (24 warps): 0 TMA, 1 MMA + TMEM owner, 2 row statistics of each
+// query tile, 4-7 dQ epilogue (and the final dK / dV store), 8-23 elementwise
+// (four groups of 4 warps, 32 query columns each).
 // The argmax correction, dK scaling and dtype casts run afterwards in the
 // shared epilogue kernels (attn_common.cu).
 
@@ -61,7 +59,8 @@ bool make_tmap_f32_rows64(CUtensorMap* map, void* base, int64_t rows, int64_t pl
 
 namespace {
 
-constexpr int kT = 128, kD = 64, kThreads = 512;
+constexpr int kT = 128, kD = 64, kThreads = 768;   // 24 warps
+constexpr int kComputeWarps = 16;
 constexpr uint32_t kTile = kT * kD * 2;       // 16 KB bf16 tile
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -90,7 +89,9 @@ struct __align__(8) BwdBarriers {
   uint64_t s_full;
   uint64_t s_free;
   uint64_t ds_ready;
-  uint64_t p_free;
+  uint64_t p_free;        // dV MMA done with P^T in TMEM
+  uint64_t ds_free[2];    // dK / dQ MMAs and the rowsum readers done with dS^T buffer b
+  uint64_t ds_full_epi[2];  // dS^T buffer b written (for the epilogue's rowsum)
   uint64_t dq_full;
   uint64_t dq_free;
   uint64_t fin;
@@ -100,19 +101,17 @@ struct __align__(8) BwdBarriers {
   float red_tau, red_alpha;
 };
 
-constexpr uint32_t kOffK = 0;                       // K tile, then the ones tile (LBO 16 KB)
-constexpr uint32_t kOffOnes = kOffK + kTile;
-constexpr uint32_t kOffV = kOffOnes + kTile;
+constexpr uint32_t kOffK = 0;
+constexpr uint32_t kOffV = kOffK + kTile;
 constexpr uint32_t kOffQ = kOffV + kTile;           // 2 stages
 constexpr uint32_t kOffDO = kOffQ + 2 * kTile;      // 2 stages
-constexpr uint32_t kOffP = kOffDO + 2 * kTile;      // P^T, 2 atoms of 64 queries
-constexpr uint32_t kOffDS = kOffP + 2 * kTile;      // dS^T, 2 atoms
-constexpr uint32_t kOffStage = kOffDS + 2 * kTile;  // dQ staging, 2 boxes [128][32] fp32
+constexpr uint32_t kOffDS = kOffDO + 2 * kTile;     // dS^T, 2 buffers x 2 atoms of 64 queries
+constexpr uint32_t kOffStage = kOffDS + 4 * kTile;  // dQ staging, 2 boxes [128][32] fp32
 constexpr uint32_t kOffStats = kOffStage + 2 * kTile;   // 2 stages x {mc, rz, dq} x 128 fp32
 constexpr uint32_t kOffBar = kOffStats + 2 * 3 * kT * 4;
 constexpr uint32_t kBwdSmem = kOffBar + sizeof(BwdBarriers) + 1024;
 
-constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
+constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 320, kColDQ = 384, kColP = 448;
 
 __device__ __forceinline__ float bwd_mask_value(const BwdParams& p, int b, int h, int r, int c) {
   float mv = 0.f;
@@ -139,20 +138,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
   const int64_t bh = static_cast<int64_t>(b) * p.H + h;
   volatile int* abort_flag = &bars->abort_flag;
 
-  // the all-ones column (n = 0 of the second B atom of the dQ MMA), MN-major SW128
-  for (int i = threadIdx.x; i < static_cast<int>(kTile / 16); i += kThreads) {
-    const int row = i >> 3, chunk = i & 7;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (chunk == (0 ^ (row & 7))) v.x = 0x3F80u;   // bf16 1.0 in element 0 of logical chunk 0
-    reinterpret_cast<uint4*>(smem + kOffOnes)[i] = v;
-  }
-  tc::fence_async_smem();
   if (threadIdx.x == 0) {
     tc::mbar_init(&bars->kv_full, 1);
-    for (int s = 0; s < 2; ++s) { tc::mbar_init(&bars->qd_full[s], 2); tc::mbar_init(&bars->qd_empty[s], 1); }
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(&bars->qd_full[s], 2);
+      tc::mbar_init(&bars->qd_empty[s], 1);
+      tc::mbar_init(&bars->ds_free[s], 1 + 4);          // MMA commit + 4 epilogue warps
+      tc::mbar_init(&bars->ds_full_epi[s], kComputeWarps);
+    }
     tc::mbar_init(&bars->s_full, 1);
-    tc::mbar_init(&bars->s_free, 8);
-    tc::mbar_init(&bars->ds_ready, 8);
+    tc::mbar_init(&bars->s_free, kComputeWarps);
+    tc::mbar_init(&bars->ds_ready, kComputeWarps);
     tc::mbar_init(&bars->p_free, 1);
     tc::mbar_init(&bars->dq_full, 1);
     tc::mbar_init(&bars->dq_free, 4);
@@ -203,10 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     if (lane == 0) {
       constexpr uint32_t idS = tc::idesc_bf16(kT, kT, 0, 0);
       constexpr uint32_t idG = tc::idesc_bf16(kT, kD, 0, 1);
-      constexpr uint32_t idQ = tc::idesc_bf16(kT, kD + 16, 1, 1);
+      constexpr uint32_t idQ = tc::idesc_bf16(kT, kD, 1, 1);
       const uint32_t sK = tc::smem_u32(smem + kOffK), sV = tc::smem_u32(smem + kOffV);
       const uint32_t sQ = tc::smem_u32(smem + kOffQ), sDO = tc::smem_u32(smem + kOffDO);
-      const uint32_t sP = tc::smem_u32(smem + kOffP), sDS = tc::smem_u32(smem + kOffDS);
+      const uint32_t sDS = tc::smem_u32(smem + kOffDS);
       bool ok = tc::mbar_wait(&bars->kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
       for (int i = 0; i <= nQ && ok; ++i) {
         if (i < nQ) {
@@ -233,26 +229,27 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           if (ok && j > 0) ok = tc::mbar_wait(&bars->dq_free, (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
           if (!ok) break;
           tc::tc_fence_after();
+          const uint32_t dsb = sDS + sj * 2 * kTile;
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk) {      // dV += P^T dO_j
-            const uint32_t pa = sP + (kk >> 2) * kTile + (kk & 3) * 32;
-            tc::umma_f16_ss(tmem + kColDV, tc::sdesc_sw128(pa, 16, 1024),
+          for (int kk = 0; kk < kT / 16; ++kk) {      // dV += P^T dO_j, P^T from TMEM
+            tc::umma_f16_ts(tmem + kColDV, tmem + kColP + kk * 8,
                             tc::sdesc_sw128(sDO + sj * kTile + kk * 2048, 16384, 1024), idG,
                             (j > 0 || kk > 0) ? 1u : 0u);
           }
+          tc::umma_commit(&bars->p_free);
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk) {      // dK += dS^T Q_j
-            const uint32_t pa = sDS + (kk >> 2) * kTile + (kk & 3) * 32;
+            const uint32_t pa = dsb + (kk >> 2) * kTile + (kk & 3) * 32;
             tc::umma_f16_ss(tmem + kColDK, tc::sdesc_sw128(pa, 16, 1024),
                             tc::sdesc_sw128(sQ + sj * kTile + kk * 2048, 16384, 1024), idG,
                             (j > 0 || kk > 0) ? 1u : 0u);
           }
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk) {      // dQ_j = dS [K | 1]
-            tc::umma_f16_ss(tmem + kColDQ, tc::sdesc_sw128(sDS + kk * 2048, 16384, 1024),
+          for (int kk = 0; kk < kT / 16; ++kk) {      // dQ_j = dS K
+            tc::umma_f16_ss(tmem + kColDQ, tc::sdesc_sw128(dsb + kk * 2048, 16384, 1024),
                             tc::sdesc_sw128(sK + kk * 2048, 16384, 1024), idQ, kk > 0);
           }
-          tc::umma_commit(&bars->p_free);
+          tc::umma_commit(&bars->ds_free[sj]);
           tc::umma_commit(&bars->qd_empty[sj]);
           tc::umma_commit(&bars->dq_full);
         }
@@ -296,171 +293,119 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     }
   } else if (warp >= 4 && warp < 8) {
     // ---------------------------------------------------------------- dQ epilogue
+    // One thread per query row; 32 TMEM columns in registers at a time.
     const int r = ((warp & 3) << 5) + lane;
+    const float ta = tau * alpha;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) << 5) << 16;
-    float* stage = reinterpret_cast<float*>(smem + kOffStage);
+    uint8_t* stage = smem + kOffStage;
     bool ok = true;
     for (int j = 0; j < nQ && ok; ++j) {
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->dq_full, j & 1, abort_flag, p.err, kErrTimeoutCompute));
+      // the previous reduce must have finished reading the staging buffer
+      if (threadIdx.x == 128) tc::bulk_wait_group_read0();
+      // one decision for the whole group (it meets again at a named barrier below)
+      ok = tc::named_barrier_and(1, 128, tc::mbar_wait(&bars->dq_full, j & 1, abort_flag, p.err,
+                                                       kErrTimeoutCompute));
       if (!ok) break;
       tc::tc_fence_after();
-      uint32_t a0[32], a1[32], a2[32];
-      tc::tmem_ld32(tmem + lane_base + kColDQ, a0);
-      tc::tmem_ld32(tmem + lane_base + kColDQ + 32, a1);
-      tc::tmem_ld32(tmem + lane_base + kColDQ + 64, a2);
-      tc::tmem_wait_ld();
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t a[32];
+        tc::tmem_ld32(tmem + lane_base + kColDQ + 32 * half, a);
+        tc::tmem_wait_ld_regs(a);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int pc = (u ^ (r & 7)) << 4;
+          *reinterpret_cast<float4*>(stage + half * kTile + r * 128 + pc) =
+              make_float4(__uint_as_float(a[4 * u]) * ta, __uint_as_float(a[4 * u + 1]) * ta,
+                          __uint_as_float(a[4 * u + 2]) * ta, __uint_as_float(a[4 * u + 3]) * ta);
+        }
+      }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->dq_free);
-      const int q = j * kT + r;
-      if (q < p.Lq) atomicAdd(p.ws_rowf + bh * p.Lq + q, __uint_as_float(a2[0]));
-      // the previous reduce must have finished reading the staging buffer
-      if (threadIdx.x == 128) tc::bulk_wait_group_read0();
-      tc::named_barrier_sync(1, 128);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int pc = (u ^ (r & 7)) << 4;
-        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(stage) + r * 128 + pc) =
-            make_uint4(a0[4 * u], a0[4 * u + 1], a0[4 * u + 2], a0[4 * u + 3]);
-        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(stage) + kTile + r * 128 + pc) =
-            make_uint4(a1[4 * u], a1[4 * u + 1], a1[4 * u + 2], a1[4 * u + 3]);
-      }
       tc::fence_async_smem();
       tc::named_barrier_sync(1, 128);
       if (threadIdx.x == 128) {
         tc::tma_reduce_add_3d(&p.tdq, stage, 0, j * kT, static_cast<int>(bh));
-        tc::tma_reduce_add_3d(&p.tdq, reinterpret_cast<uint8_t*>(stage) + kTile, 32, j * kT,
-                              static_cast<int>(bh));
+        tc::tma_reduce_add_3d(&p.tdq, stage + kTile, 32, j * kT, static_cast<int>(bh));
         tc::bulk_commit_group();
       }
+      // rowsum_keys(F) of query r from the bf16 dS^T tile (key rows, 128B-swizzled)
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->ds_full_epi[j & 1], (j >> 1) & 1, abort_flag,
+                                                  p.err, kErrTimeoutCompute));
+      if (!ok) break;
+      const uint8_t* dsb = smem + kOffDS + (j & 1) * 2 * kTile + (r >> 6) * kTile + (r & 7) * 2;
+      const int cq = (r & 63) >> 3;
+      float cs0 = 0.f, cs1 = 0.f;
+#pragma unroll 8
+      for (int k = 0; k < kT; k += 2) {
+        const uint16_t e0 = *reinterpret_cast<const uint16_t*>(dsb + k * 128 + ((cq ^ (k & 7)) << 4));
+        const uint16_t e1 = *reinterpret_cast<const uint16_t*>(dsb + (k + 1) * 128 + ((cq ^ ((k + 1) & 7)) << 4));
+        cs0 += __uint_as_float(static_cast<uint32_t>(e0) << 16);
+        cs1 += __uint_as_float(static_cast<uint32_t>(e1) << 16);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->ds_free[j & 1]);
+      const int q = j * kT + r;
+      if (q < p.Lq) atomicAdd(p.ws_rowf + bh * p.Lq + q, (cs0 + cs1) * ta);
     }
     // final dK / dV (one thread per key row)
     if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->fin, 0, abort_flag, p.err, kErrTimeoutCompute));
     if (ok) {
       tc::tc_fence_after();
-      uint32_t v0[32], v1[32];
       const int key = k0 + r;
-      tc::tmem_ld32(tmem + lane_base + kColDV, v0);
-      tc::tmem_ld32(tmem + lane_base + kColDV + 32, v1);
-      tc::tmem_wait_ld();
-      if (key < p.Lk) {
-        __nv_bfloat16* dvrow = static_cast<__nv_bfloat16*>(p.dv) + b * p.dvs[0] + h * p.dvs[1] +
-                               static_cast<int64_t>(key) * p.dvs[2];
+      __nv_bfloat16* dvrow = static_cast<__nv_bfloat16*>(p.dv) + b * p.dvs[0] + h * p.dvs[1] +
+                             static_cast<int64_t>(key) * p.dvs[2];
+      float4* dkrow = reinterpret_cast<float4*>(p.ws_dk + (bh * p.Lk + key) * kD);
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v[32];
+        tc::tmem_ld32(tmem + lane_base + kColDV + 32 * half, v);
+        tc::tmem_wait_ld_regs(v);
+        if (key < p.Lk) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          uint4 w;
-          w.x = tc::pack_bf16(__uint_as_float(v0[8 * u]), __uint_as_float(v0[8 * u + 1]));
-          w.y = tc::pack_bf16(__uint_as_float(v0[8 * u + 2]), __uint_as_float(v0[8 * u + 3]));
-          w.z = tc::pack_bf16(__uint_as_float(v0[8 * u + 4]), __uint_as_float(v0[8 * u + 5]));
-          w.w = tc::pack_bf16(__uint_as_float(v0[8 * u + 6]), __uint_as_float(v0[8 * u + 7]));
-          reinterpret_cast<uint4*>(dvrow)[u] = w;
-          w.x = tc::pack_bf16(__uint_as_float(v1[8 * u]), __uint_as_float(v1[8 * u + 1]));
-          w.y = tc::pack_bf16(__uint_as_float(v1[8 * u + 2]), __uint_as_float(v1[8 * u + 3]));
-          w.z = tc::pack_bf16(__uint_as_float(v1[8 * u + 4]), __uint_as_float(v1[8 * u + 5]));
-          w.w = tc::pack_bf16(__uint_as_float(v1[8 * u + 6]), __uint_as_float(v1[8 * u + 7]));
-          reinterpret_cast<uint4*>(dvrow)[4 + u] = w;
+          for (int u = 0; u < 4; ++u) {
+            uint4 w;
+            w.x = tc::pack_bf16(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1]));
+            w.y = tc::pack_bf16(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3]));
+            w.z = tc::pack_bf16(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5]));
+            w.w = tc::pack_bf16(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7]));
+            reinterpret_cast<uint4*>(dvrow)[4 * half + u] = w;
+          }
         }
-      }
-      tc::tmem_ld32(tmem + lane_base + kColDK, v0);
-      tc::tmem_ld32(tmem + lane_base + kColDK + 32, v1);
-      tc::tmem_wait_ld();
-      if (key < p.Lk) {
-        float4* dkrow = reinterpret_cast<float4*>(p.ws_dk + (bh * p.Lk + key) * kD);
+        tc::tmem_ld32(tmem + lane_base + kColDK + 32 * half, v);
+        tc::tmem_wait_ld_regs(v);
+        if (key < p.Lk) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          dkrow[u] = make_float4(__uint_as_float(v0[4 * u]), __uint_as_float(v0[4 * u + 1]),
-                                 __uint_as_float(v0[4 * u + 2]), __uint_as_float(v0[4 * u + 3]));
-          dkrow[8 + u] = make_float4(__uint_as_float(v1[4 * u]), __uint_as_float(v1[4 * u + 1]),
-                                     __uint_as_float(v1[4 * u + 2]), __uint_as_float(v1[4 * u + 3]));
+          for (int u = 0; u < 8; ++u)
+            dkrow[8 * half + u] = make_float4(__uint_as_float(v[4 * u]) * ta, __uint_as_float(v[4 * u + 1]) * ta,
+                                              __uint_as_float(v[4 * u + 2]) * ta, __uint_as_float(v[4 * u + 3]) * ta);
         }
       }
     }
     if (threadIdx.x == 128) tc::bulk_wait_group0();
   } else if (warp >= 8) {
     // ---------------------------------------------------------------- elementwise
-    // Per score: a2 = log2(e) alpha (s scale - m), y = tau log2 sigma (tau folded
-    // into the polynomial), q = 2^max(y, ylo) (both clamps of the reference in
-    // one), P = q / Z, t = P (dP - D), F = tau alpha t sigma'/sigma.
+    // Per score: a2 = log2(e) alpha (s scale - m), y = tau log2 sigma,
+    // q = 2^max(y, ylo) (both clamps of the reference in one), P = q / Z,
+    // t = P (dP - D), F / (tau alpha) = t sigma'/sigma.
     // Sums kept scaled: acc_tau = sum t tau log2 sigma_clamped and
     // acc_alpha = sum t clip(ratio a2, +-30 log2(e) alpha); the constants are
     // divided out once per CTA.
-    const int half = (warp - 8) >> 2;                // query columns [64 half, 64 half + 64)
+    const int grp = (warp - 8) >> 2;                 // query columns [32 grp, 32 grp + 32)
     const int r = ((warp & 3) << 5) + lane;          // key row = TMEM lane
     const int key = k0 + r;
     const bool key_ok = key < p.Lk;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) << 5) << 16;
     const float al2 = alpha * kLog2e;
-    const float sa2 = p.scale * al2, ta = tau * alpha;
+    const float sa2 = p.scale * al2;
     const float ylo = fmaxf(tau * kLog2Clamp, kLog2Clamp);
     const float ytau = tau * kLog2Clamp;
     const float glim = 30.f * al2;
     const float kmask = key_ok ? 1.f : 0.f;
     const bool has_mask = p.mask != nullptr || p.causal;
-    uint8_t* Pt = smem + kOffP + half * kTile;
-    uint8_t* DSt = smem + kOffDS + half * kTile;
     float acc_tau = 0.f, acc_alpha = 0.f;
     bool ok = true;
-    // 16 query columns: scores sv, dP dv -> packed bf16 P (pp) and F (pf)
-    auto chunk16 = [&](const uint32_t* sv, const uint32_t* dv, const float* st, int col0, int i,
-                       uint32_t* pp, uint32_t* pf) {
-#pragma unroll
-      for (int e4 = 0; e4 < 16; e4 += 4) {
-        const float4 mc4 = *reinterpret_cast<const float4*>(st + col0 + e4);
-        const float4 rz4 = *reinterpret_cast<const float4*>(st + kT + col0 + e4);
-        const float4 dq4 = *reinterpret_cast<const float4*>(st + 2 * kT + col0 + e4);
-        const float mc[4] = {mc4.x, mc4.y, mc4.z, mc4.w};
-        const float rz[4] = {rz4.x, rz4.y, rz4.z, rz4.w};
-        const float dq[4] = {dq4.x, dq4.y, dq4.z, dq4.w};
-        float P4[4], F4[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = e4 + u;
-          float a2 = fmaf(__uint_as_float(sv[e]), sa2, mc[u]);
-          if (has_mask) {
-            const int q = i * kT + col0 + e;
-            if (key_ok && q < p.Lq) a2 = fmaf(bwd_mask_value(p, b, h, q, key), al2, a2);
-          }
-          float y, ratio;
-          if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
-            const float ex = tc::ex2(a2);
-            y = fmaf(tau, a2, poly::G_scaled(ex, tau));
-            ratio = poly::R(ex);
-          } else if (SIG == TAU_DXB_SIGMA_SIGMOID) {
-            const float ex = tc::ex2(a2);
-            y = fmaf(tau, a2, -poly::H_scaled(ex, tau));
-            ratio = poly::S(ex);
-          } else if (SIG == TAU_DXB_SIGMA_EXP) {
-            y = tau * a2;
-            ratio = 1.f;
-          } else {
-            y = ytau;
-            ratio = 1.f;
-          }
-          const float qv = tc::ex2(fmaxf(y, ylo));
-          const float P = qv * rz[u] * kmask;
-          const float t = P * (__uint_as_float(dv[e]) - dq[u]);
-          acc_tau = fmaf(t, fmaxf(y, ytau), acc_tau);
-          acc_alpha = fmaf(t, fminf(fmaxf(ratio * a2, -glim), glim), acc_alpha);
-          P4[u] = P;
-          F4[u] = ta * (t * ratio);
-        }
-        pp[e4 >> 1] = tc::pack_bf16(P4[0], P4[1]);
-        pp[(e4 >> 1) + 1] = tc::pack_bf16(P4[2], P4[3]);
-        pf[e4 >> 1] = tc::pack_bf16(F4[0], F4[1]);
-        pf[(e4 >> 1) + 1] = tc::pack_bf16(F4[2], F4[3]);
-      }
-    };
-    // P^T / dS^T rows: key r, 16 queries = two 16-byte chunks of the 64-query atom
-    auto store16 = [&](int c, const uint32_t* pp, const uint32_t* pf) {
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int chunk = ((c * 2 + u) ^ (r & 7)) << 4;
-        *reinterpret_cast<uint4*>(Pt + r * 128 + chunk) =
-            make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
-        *reinterpret_cast<uint4*>(DSt + r * 128 + chunk) =
-            make_uint4(pf[4 * u], pf[4 * u + 1], pf[4 * u + 2], pf[4 * u + 3]);
-      }
-    };
     for (int i = 0; i < nQ && ok; ++i) {
       const int s = i & 1;
       ok = tc::mbar_wait(&bars->qd_full[s], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutCompute);
@@ -469,41 +414,96 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       if (!ok) break;
       tc::tc_fence_after();
       const float* st = stats + s * 3 * kT;
-      const uint32_t tS = tmem + lane_base + kColS + half * 64;
-      const uint32_t tP = tmem + lane_base + kColDP + half * 64;
-      uint32_t ra[32], rb[32];     // [0,16) scores, [16,32) dP of one 16-column chunk
-      tc::tmem_ld16(tS, ra);
-      tc::tmem_ld16(tP, ra + 16);
-      tc::tmem_wait_ld_regs(ra);
-      bool pfree_ok = true;
+      uint8_t* DSt = smem + kOffDS + s * 2 * kTile + (grp >> 1) * kTile;   // this group's 64-query atom
 #pragma unroll 1
-      for (int c = 0; c < 4; c += 2) {
-        tc::tmem_ld16(tS + (c + 1) * 16, rb);                 // next chunk in flight
-        tc::tmem_ld16(tP + (c + 1) * 16, rb + 16);
-        uint32_t pp[8], pf[8];
-        chunk16(ra, ra + 16, st, half * 64 + c * 16, i, pp, pf);
-        if (c == 0 && i > 0)   // the previous tile's MMAs must be done with P^T / dS^T
-          pfree_ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->p_free, (i - 1) & 1, abort_flag,
-                                                          p.err, kErrTimeoutCompute));
-        if (pfree_ok) store16(c, pp, pf);
-        tc::tmem_wait_ld_regs(rb);
-        if (c + 2 < 4) {
-          tc::tmem_ld16(tS + (c + 2) * 16, ra);
-          tc::tmem_ld16(tP + (c + 2) * 16, ra + 16);
-        } else {        // every TMEM read of this tile is done
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = grp * 32 + c * 16;
+        uint32_t rr[32];     // [0,16) scores, [16,32) dP of 16 query columns
+        tc::tmem_ld16(tmem + lane_base + kColS + col0, rr);
+        tc::tmem_ld16(tmem + lane_base + kColDP + col0, rr + 16);
+        tc::tmem_wait_ld_regs(rr);
+        if (c == 1) {        // every TMEM read of this tile is done
           tc::tc_fence_before();
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(&bars->s_free);
         }
-        chunk16(rb, rb + 16, st, half * 64 + (c + 1) * 16, i, pp, pf);
-        if (pfree_ok) store16(c + 1, pp, pf);
-        if (c + 2 < 4) tc::tmem_wait_ld_regs(ra);
+        uint32_t pp[8], pf[8];
+        float fsum[16];
+#pragma unroll
+        for (int e4 = 0; e4 < 16; e4 += 4) {
+          const float4 mc4 = *reinterpret_cast<const float4*>(st + col0 + e4);
+          const float4 rz4 = *reinterpret_cast<const float4*>(st + kT + col0 + e4);
+          const float4 dq4 = *reinterpret_cast<const float4*>(st + 2 * kT + col0 + e4);
+          const float mc[4] = {mc4.x, mc4.y, mc4.z, mc4.w};
+          const float rz[4] = {rz4.x, rz4.y, rz4.z, rz4.w};
+          const float dq[4] = {dq4.x, dq4.y, dq4.z, dq4.w};
+          float P4[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int e = e4 + u;
+            float a2 = fmaf(__uint_as_float(rr[e]), sa2, mc[u]);
+            if (has_mask) {
+              const int q = i * kT + col0 + e;
+              if (key_ok && q < p.Lq) a2 = fmaf(bwd_mask_value(p, b, h, q, key), al2, a2);
+            }
+            float y, ratio;
+            if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
+              const float ex = tc::ex2(a2);
+              y = tau * (a2 + poly::G(ex));
+              ratio = poly::R(ex);
+            } else if (SIG == TAU_DXB_SIGMA_SIGMOID) {
+              const float ex = tc::ex2(a2);
+              y = tau * (a2 - poly::H(ex));
+              ratio = poly::S(ex);
+            } else if (SIG == TAU_DXB_SIGMA_EXP) {
+              y = tau * a2;
+              ratio = 1.f;
+            } else {
+              y = ytau;
+              ratio = 1.f;
+            }
+            const float qv = tc::ex2(fmaxf(y, ylo));
+            const float P = qv * rz[u] * kmask;
+            const float t = P * (__uint_as_float(rr[16 + e]) - dq[u]);
+            acc_tau = fmaf(t, fmaxf(y, ytau), acc_tau);
+            acc_alpha = fmaf(t, fminf(fmaxf(ratio * a2, -glim), glim), acc_alpha);
+            P4[u] = P;
+            fsum[e] = t * ratio;
+          }
+          pp[e4 >> 1] = tc::pack_bf16(P4[0], P4[1]);
+          pp[(e4 >> 1) + 1] = tc::pack_bf16(P4[2], P4[3]);
+        }
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) pf[e >> 1] = tc::pack_bf16(fsum[e], fsum[e + 1]);
+        if (c == 0) {
+          // P^T in TMEM is free once the previous tile's dV MMA is done, the dS^T
+          // buffer once the MMAs of the tile two back are done with it
+          bool fr = i == 0 || tc::mbar_wait(&bars->p_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutCompute);
+          if (fr && i >= 2) fr = tc::mbar_wait(&bars->ds_free[s], ((i >> 1) - 1) & 1, abort_flag, p.err,
+                                               kErrTimeoutCompute);
+          ok = __all_sync(0xffffffffu, fr);
+          if (!ok) break;
+          tc::tc_fence_after();
+        }
+        // P^T: 16 queries = 8 packed columns of this lane's TMEM row
+        tc::tmem_st8(tmem + lane_base + kColP + (col0 >> 1), pp);
+        // dS^T row: key r, 16 queries = two 16-byte chunks of the 64-query atom
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int chunk = (((grp & 1) * 4 + c * 2 + u) ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(DSt + r * 128 + chunk) =
+              make_uint4(pf[4 * u], pf[4 * u + 1], pf[4 * u + 2], pf[4 * u + 3]);
+        }
       }
-      ok = pfree_ok;
       if (!ok) break;
+      tc::tmem_wait_st();
       tc::fence_async_smem();
+      tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars->ds_ready);
+      if (lane == 0) {
+        tc::mbar_arrive(&bars->ds_ready);
+        tc::mbar_arrive(&bars->ds_full_epi[s]);
+      }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
