@@ -200,9 +200,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       constexpr uint32_t idS = tc::idesc_bf16(kT, kT, 0, 0);
       constexpr uint32_t idG = tc::idesc_bf16(kT, kD, 0, 1);
       constexpr uint32_t idQ = tc::idesc_bf16(kT, kD, 1, 1);
+      // descriptor low halves; K-major operands step 32 B (2) per K slice of 16,
+      // MN-major ones 2048 B (128), the high half is the same for both layouts
+      constexpr uint32_t hi = tc::sdesc_hi_sw128(1024);
       const uint32_t sK = tc::smem_u32(smem + kOffK), sV = tc::smem_u32(smem + kOffV);
       const uint32_t sQ = tc::smem_u32(smem + kOffQ), sDO = tc::smem_u32(smem + kOffDO);
       const uint32_t sDS = tc::smem_u32(smem + kOffDS);
+      const uint32_t kK = tc::sdesc_lo(sK, 16), kV = tc::sdesc_lo(sV, 16), mK = tc::sdesc_lo(sK, 16384);
+      constexpr uint32_t tileStep = kTile >> 4;
       bool ok = tc::mbar_wait(&bars->kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
       for (int i = 0; i <= nQ && ok; ++i) {
         if (i < nQ) {
@@ -211,16 +216,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           if (ok && i > 0) ok = tc::mbar_wait(&bars->s_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
           if (!ok) break;
           tc::tc_fence_after();
+          const uint32_t kQ = tc::sdesc_lo(sQ, 16) + s * tileStep, kDO = tc::sdesc_lo(sDO, 16) + s * tileStep;
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            tc::umma_f16_ss(tmem + kColS, tc::sdesc_sw128(sK + kk * 32, 16, 1024),
-                            tc::sdesc_sw128(sQ + s * kTile + kk * 32, 16, 1024), idS, kk > 0);
-          }
+          for (int kk = 0; kk < kD / 16; ++kk)
+            tc::umma_f16_ss2(tmem + kColS, kK + 2 * kk, hi, kQ + 2 * kk, hi, idS, kk > 0);
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            tc::umma_f16_ss(tmem + kColDP, tc::sdesc_sw128(sV + kk * 32, 16, 1024),
-                            tc::sdesc_sw128(sDO + s * kTile + kk * 32, 16, 1024), idS, kk > 0);
-          }
+          for (int kk = 0; kk < kD / 16; ++kk)
+            tc::umma_f16_ss2(tmem + kColDP, kV + 2 * kk, hi, kDO + 2 * kk, hi, idS, kk > 0);
           tc::umma_commit(&bars->s_full);
         }
         if (i > 0) {
@@ -229,26 +231,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           if (ok && j > 0) ok = tc::mbar_wait(&bars->dq_free, (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
           if (!ok) break;
           tc::tc_fence_after();
-          const uint32_t dsb = sDS + sj * 2 * kTile;
+          const uint32_t mDO = tc::sdesc_lo(sDO, 16384) + sj * tileStep;
+          const uint32_t mQ = tc::sdesc_lo(sQ, 16384) + sj * tileStep;
+          const uint32_t kDS = tc::sdesc_lo(sDS, 16) + sj * 2 * tileStep;
+          const uint32_t mDS = tc::sdesc_lo(sDS, 16384) + sj * 2 * tileStep;
+          const bool acc0 = j > 0;
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk) {      // dV += P^T dO_j, P^T from TMEM
-            tc::umma_f16_ts(tmem + kColDV, tmem + kColP + kk * 8,
-                            tc::sdesc_sw128(sDO + sj * kTile + kk * 2048, 16384, 1024), idG,
-                            (j > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < kT / 16; ++kk)      // dV += P^T dO_j, P^T from TMEM
+            tc::umma_f16_ts2(tmem + kColDV, tmem + kColP + kk * 8, mDO + 128 * kk, hi, idG, acc0 || kk > 0);
           tc::umma_commit(&bars->p_free);
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk) {      // dK += dS^T Q_j
-            const uint32_t pa = dsb + (kk >> 2) * kTile + (kk & 3) * 32;
-            tc::umma_f16_ss(tmem + kColDK, tc::sdesc_sw128(pa, 16, 1024),
-                            tc::sdesc_sw128(sQ + sj * kTile + kk * 2048, 16384, 1024), idG,
-                            (j > 0 || kk > 0) ? 1u : 0u);
-          }
+          for (int kk = 0; kk < kT / 16; ++kk)      // dK += dS^T Q_j
+            tc::umma_f16_ss2(tmem + kColDK, kDS + (kk >> 2) * tileStep + (kk & 3) * 2, hi, mQ + 128 * kk, hi,
+                             idG, acc0 || kk > 0);
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk) {      // dQ_j = dS K
-            tc::umma_f16_ss(tmem + kColDQ, tc::sdesc_sw128(dsb + kk * 2048, 16384, 1024),
-                            tc::sdesc_sw128(sK + kk * 2048, 16384, 1024), idQ, kk > 0);
-          }
+          for (int kk = 0; kk < kT / 16; ++kk)      // dQ_j = dS K
+            tc::umma_f16_ss2(tmem + kColDQ, mDS + 128 * kk, hi, mK + 128 * kk, hi, idQ, kk > 0);
           tc::umma_commit(&bars->ds_free[sj]);
           tc::umma_commit(&bars->qd_empty[sj]);
           tc::umma_commit(&bars->dq_full);
@@ -334,20 +332,36 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->ds_full_epi[j & 1], (j >> 1) & 1, abort_flag,
                                                   p.err, kErrTimeoutCompute));
       if (!ok) break;
-      const uint8_t* dsb = smem + kOffDS + (j & 1) * 2 * kTile + (r >> 6) * kTile + (r & 7) * 2;
-      const int cq = (r & 63) >> 3;
-      float cs0 = 0.f, cs1 = 0.f;
-#pragma unroll 8
-      for (int k = 0; k < kT; k += 2) {
-        const uint16_t e0 = *reinterpret_cast<const uint16_t*>(dsb + k * 128 + ((cq ^ (k & 7)) << 4));
-        const uint16_t e1 = *reinterpret_cast<const uint16_t*>(dsb + (k + 1) * 128 + ((cq ^ ((k + 1) & 7)) << 4));
-        cs0 += __uint_as_float(static_cast<uint32_t>(e0) << 16);
-        cs1 += __uint_as_float(static_cast<uint32_t>(e1) << 16);
+      // thread r: 8 queries (16-byte chunk c8 of 64-query atom r>>6) over the
+      // 16 key rows kp, kp+8, ...; in a 128B-swizzled row k the chunk sits at
+      // c8 ^ (k & 7) = c8 ^ kp, the same for all 16 rows
+      const int c8 = (r >> 3) & 7, kp = r & 7;
+      const uint8_t* dsb = smem + kOffDS + (j & 1) * 2 * kTile + (r >> 6) * kTile + kp * 128 + ((c8 ^ kp) << 4);
+      float2 cs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int m = 0; m < kT / 8; ++m) {
+        const uint4 w = *reinterpret_cast<const uint4*>(dsb + m * 1024);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          cs[u] = tc::add2(cs[u], make_float2(__uint_as_float(ws[u] << 16), __uint_as_float(ws[u] & 0xffff0000u)));
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->ds_free[j & 1]);
-      const int q = j * kT + r;
-      if (q < p.Lq) atomicAdd(p.ws_rowf + bh * p.Lq + q, (cs0 + cs1) * ta);
+      // reduce over the 8 lanes kp = 0..7 of this chunk; lane kp ends with query 8 c8 + kp
+      float v[8] = {cs[0].x, cs[0].y, cs[1].x, cs[1].y, cs[2].x, cs[2].y, cs[3].x, cs[3].y};
+#pragma unroll
+      for (int lvl = 4; lvl >= 1; lvl >>= 1) {
+        const bool upper = (kp & lvl) != 0;
+#pragma unroll
+        for (int u = 0; u < lvl; ++u) {
+          const float send = upper ? v[u] : v[u + lvl];
+          const float keep = upper ? v[u + lvl] : v[u];
+          v[u] = keep + __shfl_xor_sync(0xffffffffu, send, lvl);
+        }
+      }
+      const int q = j * kT + (r >> 6) * 64 + c8 * 8 + kp;
+      if (q < p.Lq) atomicAdd(p.ws_rowf + bh * p.Lq + q, v[0] * ta);
     }
     // final dK / dV (one thread per key row)
     if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->fin, 0, abort_flag, p.err, kErrTimeoutCompute));
@@ -403,8 +417,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     const float ytau = tau * kLog2Clamp;
     const float glim = 30.f * al2;
     const float kmask = key_ok ? 1.f : 0.f;
+    const float2 kmask2 = make_float2(kmask, kmask), sa2x2 = make_float2(sa2, sa2);
+    const float2 taux2 = make_float2(tau, tau);
+    const bool tile_full = k0 + kT <= p.Lk;
     const bool has_mask = p.mask != nullptr || p.causal;
-    float acc_tau = 0.f, acc_alpha = 0.f;
+    float2 acc_tau = make_float2(0.f, 0.f), acc_alpha = make_float2(0.f, 0.f);
     bool ok = true;
     for (int i = 0; i < nQ && ok; ++i) {
       const int s = i & 1;
@@ -428,53 +445,53 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           if (lane == 0) tc::mbar_arrive(&bars->s_free);
         }
         uint32_t pp[8], pf[8];
-        float fsum[16];
 #pragma unroll
         for (int e4 = 0; e4 < 16; e4 += 4) {
           const float4 mc4 = *reinterpret_cast<const float4*>(st + col0 + e4);
           const float4 rz4 = *reinterpret_cast<const float4*>(st + kT + col0 + e4);
           const float4 dq4 = *reinterpret_cast<const float4*>(st + 2 * kT + col0 + e4);
-          const float mc[4] = {mc4.x, mc4.y, mc4.z, mc4.w};
-          const float rz[4] = {rz4.x, rz4.y, rz4.z, rz4.w};
-          const float dq[4] = {dq4.x, dq4.y, dq4.z, dq4.w};
-          float P4[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int e = e4 + u;
-            float a2 = fmaf(__uint_as_float(rr[e]), sa2, mc[u]);
+          for (int h2 = 0; h2 < 2; ++h2) {      // a pair of query columns per f32x2 lane pair
+            const int e = e4 + 2 * h2;
+            const float2 mc = h2 ? make_float2(mc4.z, mc4.w) : make_float2(mc4.x, mc4.y);
+            const float2 rz = h2 ? make_float2(rz4.z, rz4.w) : make_float2(rz4.x, rz4.y);
+            const float2 dq = h2 ? make_float2(dq4.z, dq4.w) : make_float2(dq4.x, dq4.y);
+            float2 a2 = tc::fma2(make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), sa2x2, mc);
             if (has_mask) {
               const int q = i * kT + col0 + e;
-              if (key_ok && q < p.Lq) a2 = fmaf(bwd_mask_value(p, b, h, q, key), al2, a2);
+              if (key_ok && q < p.Lq) a2.x = fmaf(bwd_mask_value(p, b, h, q, key), al2, a2.x);
+              if (key_ok && q + 1 < p.Lq) a2.y = fmaf(bwd_mask_value(p, b, h, q + 1, key), al2, a2.y);
             }
-            float y, ratio;
-            if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
-              const float ex = tc::ex2(a2);
-              y = tau * (a2 + poly::G(ex));
-              ratio = poly::R(ex);
-            } else if (SIG == TAU_DXB_SIGMA_SIGMOID) {
-              const float ex = tc::ex2(a2);
-              y = tau * (a2 - poly::H(ex));
-              ratio = poly::S(ex);
+            float2 y, ratio;
+            if (SIG == TAU_DXB_SIGMA_SOFTPLUS || SIG == TAU_DXB_SIGMA_SIGMOID) {
+              const float ex0 = tc::ex2(a2.x), ex1 = tc::ex2(a2.y);
+              if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
+                y = tc::mul2(taux2, tc::add2(a2, make_float2(poly::G(ex0), poly::G(ex1))));
+                ratio = make_float2(poly::R(ex0), poly::R(ex1));
+              } else {
+                y = tc::mul2(taux2, tc::sub2(a2, make_float2(poly::H(ex0), poly::H(ex1))));
+                ratio = make_float2(poly::S(ex0), poly::S(ex1));
+              }
             } else if (SIG == TAU_DXB_SIGMA_EXP) {
-              y = tau * a2;
-              ratio = 1.f;
+              y = tc::mul2(taux2, a2);
+              ratio = make_float2(1.f, 1.f);
             } else {
-              y = ytau;
-              ratio = 1.f;
+              y = make_float2(ytau, ytau);
+              ratio = make_float2(1.f, 1.f);
             }
-            const float qv = tc::ex2(fmaxf(y, ylo));
-            const float P = qv * rz[u] * kmask;
-            const float t = P * (__uint_as_float(rr[16 + e]) - dq[u]);
-            acc_tau = fmaf(t, fmaxf(y, ytau), acc_tau);
-            acc_alpha = fmaf(t, fminf(fmaxf(ratio * a2, -glim), glim), acc_alpha);
-            P4[u] = P;
-            fsum[e] = t * ratio;
+            float2 P = tc::mul2(make_float2(tc::ex2(fmaxf(y.x, ylo)), tc::ex2(fmaxf(y.y, ylo))), rz);
+            if (!tile_full) P = tc::mul2(P, kmask2);
+            const float2 t = tc::mul2(P, tc::sub2(make_float2(__uint_as_float(rr[16 + e]),
+                                                              __uint_as_float(rr[17 + e])), dq));
+            acc_tau = tc::fma2(t, make_float2(fmaxf(y.x, ytau), fmaxf(y.y, ytau)), acc_tau);
+            // x = s - rowmax <= 0, so ratio * a2 <= 0: only the lower clip can act
+            const float2 ra = tc::mul2(ratio, a2);
+            acc_alpha = tc::fma2(t, make_float2(fmaxf(ra.x, -glim), fmaxf(ra.y, -glim)), acc_alpha);
+            const float2 F = tc::mul2(t, ratio);
+            pp[e >> 1] = tc::pack_bf16(P.x, P.y);
+            pf[e >> 1] = tc::pack_bf16(F.x, F.y);
           }
-          pp[e4 >> 1] = tc::pack_bf16(P4[0], P4[1]);
-          pp[(e4 >> 1) + 1] = tc::pack_bf16(P4[2], P4[3]);
         }
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) pf[e >> 1] = tc::pack_bf16(fsum[e], fsum[e + 1]);
         if (c == 0) {
           // P^T in TMEM is free once the previous tile's dV MMA is done, the dS^T
           // buffer once the MMAs of the tile two back are done with it
@@ -505,14 +522,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         tc::mbar_arrive(&bars->ds_full_epi[s]);
       }
     }
+    float sum_tau = acc_tau.x + acc_tau.y, sum_alpha = acc_alpha.x + acc_alpha.y;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
-      acc_tau += __shfl_xor_sync(0xffffffffu, acc_tau, off);
-      acc_alpha += __shfl_xor_sync(0xffffffffu, acc_alpha, off);
+      sum_tau += __shfl_xor_sync(0xffffffffu, sum_tau, off);
+      sum_alpha += __shfl_xor_sync(0xffffffffu, sum_alpha, off);
     }
     if (lane == 0) {
-      atomicAdd(&bars->red_tau, acc_tau);
-      atomicAdd(&bars->red_alpha, acc_alpha);
+      atomicAdd(&bars->red_tau, sum_tau);
+      atomicAdd(&bars->red_alpha, sum_alpha);
     }
   }
   tc::tc_fence_before();
