@@ -24,6 +24,8 @@
 // reference collapse into one. TMEM loads are double-buffered: the next
 // 32-column chunk is in flight while the current one is processed.
 
+#include <cmath>
+
 #include "attn.h"
 #include "poly_coeffs.h"
 #include "tc_common.cuh"
@@ -94,8 +96,9 @@ struct __align__(8) FwdBarriers {
   uint64_t q_full;
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t sp_ready[2];
+  uint64_t s_full[2];     // S_t in TMEM (and, in pass 2, the previous PV_t done with P_t)
+  uint64_t s_free[2];     // S_t read out of TMEM by its softmax group
+  uint64_t sp_ready[2];   // P_t written to shared memory (pass 2)
   uint64_t o_full[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -119,6 +122,8 @@ __device__ __forceinline__ float fwd_mask_value(const FwdParams& p, int b, int h
   return mv;
 }
 
+template <int V> struct IntC { static constexpr int value = V; };
+
 template <int SIG>
 __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -136,6 +141,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
     for (int s = 0; s < kStages; ++s) { tc::mbar_init(&bars->kv_full[s], 1); tc::mbar_init(&bars->kv_empty[s], 1); }
     for (int t = 0; t < 2; ++t) {
       tc::mbar_init(&bars->s_full[t], 1);
+      tc::mbar_init(&bars->s_free[t], 4);
       tc::mbar_init(&bars->sp_ready[t], 4);
       tc::mbar_init(&bars->o_full[t], 1);
     }
@@ -195,62 +201,60 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
       const uint32_t sP = tc::smem_u32(smem + kSmemP);
       bool ok = tc::mbar_wait(&bars->q_full, 0, abort_flag, p.err, kErrTimeoutMma);
       tc::tc_fence_after();
-      int it = 0, i = 0, s_prev = 0;
+      int s_prev = 0;
+      // descriptors as 32-bit halves: K-slices of 16 step 32 B (2) in K-major
+      // tiles and 2048 B (128) in the MN-major V tile; the high half is shared
+      constexpr uint32_t hi = tc::sdesc_hi_sw128(1024);
+      constexpr uint32_t tileStep = kTileBytes >> 4;
+      const uint32_t kQ = tc::sdesc_lo(sQ, 16), kK = tc::sdesc_lo(sK, 16);
+      const uint32_t kP = tc::sdesc_lo(sP, 16), mV = tc::sdesc_lo(sV, 16384);
       auto issue_S = [&](int t, int s) {
         const uint32_t d = tmem + t * kBN;
+        const uint32_t qa = kQ + t * tileStep, kb = kK + s * tileStep;
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint64_t a = tc::sdesc_sw128(sQ + t * kTileBytes + kk * 32, 16, 1024);
-          const uint64_t bb = tc::sdesc_sw128(sK + s * kTileBytes + kk * 32, 16, 1024);
-          tc::umma_f16_ss(d, a, bb, idS, kk > 0);
-        }
+        for (int kk = 0; kk < kD / 16; ++kk) tc::umma_f16_ss2(d, qa + 2 * kk, hi, kb + 2 * kk, hi, idS, kk > 0);
       };
       auto issue_PV = [&](int t, int s, bool first) {
         const uint32_t d = tmem + 256 + t * kD;
+        const uint32_t pa = kP + t * 2 * tileStep, vb = mV + s * tileStep;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint32_t pa = sP + t * 2 * kTileBytes + (kk >> 2) * kTileBytes + (kk & 3) * 32;
-          const uint64_t a = tc::sdesc_sw128(pa, 16, 1024);
-          const uint64_t bb = tc::sdesc_sw128(sV + s * kTileBytes + kk * 2048, 16384, 1024);
-          tc::umma_f16_ss(d, a, bb, idO, (!first || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          tc::umma_f16_ss2(d, pa + (kk >> 2) * tileStep + (kk & 3) * 2, hi, vb + 128 * kk, hi, idO,
+                           !first || kk > 0);
       };
-      // pass 1: S only
-      for (int j = 0; j < nK && ok; ++j, ++it, ++i) {
-        const int s = it % kStages;
-        ok = tc::mbar_wait(&bars->kv_full[s], (it / kStages) & 1, abort_flag, p.err, kErrTimeoutMma);
+      // Step i (pass 1: key tile i; pass 2: key tile i - nK): S_t into TMEM
+      // once group t has read the previous S_t out; in pass 2 then PV_t of the
+      // previous key tile once P_t is written, and s_full_t covers both (the
+      // group overwrites P_t only after that PV is done).
+      for (int i = 0; i < 2 * nK && ok; ++i) {
+        const bool pass2 = i >= nK;
+        const int j = pass2 ? i - nK : i;
+        const int s = i % kStages;
+        ok = tc::mbar_wait(&bars->kv_full[s], (i / kStages) & 1, abort_flag, p.err, kErrTimeoutMma);
         if (!ok) break;
         tc::tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
+        for (int t = 0; t < 2 && ok; ++t) {      // group 0 runs ahead of group 1
           if (i > 0) {
-            ok = tc::mbar_wait(&bars->sp_ready[t], (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
+            ok = tc::mbar_wait(&bars->s_free[t], (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
             if (!ok) break;
             tc::tc_fence_after();
           }
           issue_S(t, s);
+          if (pass2 && j > 0) {
+            ok = tc::mbar_wait(&bars->sp_ready[t], (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
+            if (!ok) break;
+            tc::tc_fence_after();
+            issue_PV(t, s_prev, j == 1);
+          }
           tc::umma_commit(&bars->s_full[t]);
         }
-        tc::umma_commit(&bars->kv_empty[s]);
-      }
-      // pass 2: S, then PV of the previous key tile
-      for (int j = 0; j < nK && ok; ++j, ++it, ++i) {
-        const int s = it % kStages;
-        ok = tc::mbar_wait(&bars->kv_full[s], (it / kStages) & 1, abort_flag, p.err, kErrTimeoutMma);
         if (!ok) break;
-        tc::tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
-          ok = tc::mbar_wait(&bars->sp_ready[t], (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
-          if (!ok) break;
-          tc::tc_fence_after();
-          if (j > 0) issue_PV(t, s_prev, j == 1);
-          issue_S(t, s);
-          tc::umma_commit(&bars->s_full[t]);
-        }
-        if (j > 0) tc::umma_commit(&bars->kv_empty[s_prev]);
-        s_prev = s;
+        if (pass2 && j > 0) tc::umma_commit(&bars->kv_empty[s_prev]);
+        if (!pass2) tc::umma_commit(&bars->kv_empty[s]);
+        else s_prev = s;
       }
       for (int t = 0; t < 2 && ok; ++t) {
-        ok = tc::mbar_wait(&bars->sp_ready[t], (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
+        ok = tc::mbar_wait(&bars->sp_ready[t], (nK - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
         if (!ok) break;
         tc::tc_fence_after();
         issue_PV(t, s_prev, nK == 1);
@@ -275,59 +279,97 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
     const uint32_t tS = tmem + lane_base + t * kBN;
     const uint32_t tO = tmem + lane_base + 256 + t * kD;
     const float tau = p.tau[h], alpha = p.alpha[h];
-    const bool has_mask = p.mask != nullptr || p.causal;
+    const bool explicit_mask = p.mask != nullptr;
+    // keys >= lim_c of this row are causally masked (score + finfo.min), keys
+    // >= Lk are padding (no contribution at all)
+    const int lim_c = p.causal ? min(p.Lk, grow + (p.Lk - p.Lq) + 1) : p.Lk;
     uint8_t* Pt = smem + kSmemP + t * 2 * kTileBytes;
     bool ok = true;
     int i = 0;
     float m = -INFINITY;
     int amax = 0;
-    // pass 1: exact row max and first argmax (scores in increasing key order;
-    // a later chunk replaces the running max only if strictly larger)
-    auto pass1_chunk = [&](const uint32_t (&v)[32], int key0, bool fast) {
-      if (fast) {
-        float cm = -INFINITY;
+    // Per key tile the warp takes one of three branch-free element paths:
+    // kFast (every key valid and unmasked for all 32 rows, no mask tensor,
+    // scale > 0), kLimited (causal limit / padding per row, no mask tensor),
+    // kGeneral (mask tensor).
+    constexpr int kFast = 0, kLimited = 1, kGeneral = 2;
+    auto tile_mode = [&](int j) -> int {
+      if (explicit_mask) return kGeneral;
+      const bool full = (j + 1) * kBN <= lim_c && p.scale > 0.f;
+      return __all_sync(0xffffffffu, full) ? kFast : kLimited;
+    };
+    // pass 1: exact row max and first argmax of s = scale * QK^T (+ mask) in
+    // increasing key order. The chunk max comes from four independent fmax
+    // chains; only when it beats the running max is the first index found.
+    // Pass 1: per 32-key chunk, four interleaved chains (keys e = a mod 4) keep
+    // their max and its first key (strictly larger replaces), so the first
+    // argmax costs no data-dependent branch. The fast path compares the raw
+    // QK^T values (scale > 0 keeps their order).
+    auto pass1_chunk = [&](auto mode_c, const uint32_t (&v)[32], int key0) {
+      constexpr int kMode = decltype(mode_c)::value;
+      float x[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) cm = fmaxf(cm, __uint_as_float(v[e]) * p.scale);
-        if (cm > m) {
-          int first = 0;
-#pragma unroll
-          for (int e = 31; e >= 0; --e)
-            if (__uint_as_float(v[e]) * p.scale == cm) first = e;
-          m = cm;
-          amax = key0 + first;
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = key0 + e;
-          if (key < p.Lk) {
-            float sv = __uint_as_float(v[e]) * p.scale;
-            if (has_mask && row_ok) sv += fwd_mask_value(p, b, h, grow, key);
-            if (sv > m) { m = sv; amax = key; }
+      for (int e = 0; e < 32; ++e) {
+        const float raw = __uint_as_float(v[e]);
+        if constexpr (kMode == kFast) {
+          x[e] = raw;
+        } else {
+          float sv = raw * p.scale;
+          if constexpr (kMode == kLimited) {
+            if (key0 + e >= lim_c) sv += kMaskMin;
+          } else {
+            if (row_ok) sv += fwd_mask_value(p, b, h, grow, key0 + e);
           }
+          x[e] = key0 + e < p.Lk ? sv : -INFINITY;
         }
       }
+      float c4[4] = {x[0], x[1], x[2], x[3]};
+      int i4[4] = {0, 1, 2, 3};
+#pragma unroll
+      for (int e = 4; e < 32; ++e) {
+        const bool gt = x[e] > c4[e & 3];
+        c4[e & 3] = gt ? x[e] : c4[e & 3];
+        i4[e & 3] = gt ? e : i4[e & 3];
+      }
+      // combine: the largest value, the smallest key among the chains holding it
+      float cx = fmaxf(fmaxf(c4[0], c4[1]), fmaxf(c4[2], c4[3]));
+      int first = 32;
+#pragma unroll
+      for (int a4 = 0; a4 < 4; ++a4) first = min(first, c4[a4] == cx ? i4[a4] : 32);
+      const float cm = kMode == kFast ? cx * p.scale : cx;
+      if (cm > m && first < 32) {           // strictly larger: earlier chunks win ties
+        m = cm;
+        amax = key0 + first;
+      }
+    };
+    auto release_s = [&]() {      // every TMEM read of S for this step is done
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->s_free[t]);
     };
     for (int j = 0; j < nK && ok; ++j, ++i) {
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->s_full[t], i & 1, abort_flag, p.err, kErrTimeoutSoftmax));
       if (!ok) break;
       tc::tc_fence_after();
-      const bool fast = (j + 1) * kBN <= p.Lk && !has_mask;
-      uint32_t va[32], vb[32];
-      tc::tmem_ld32(tS, va);
-      tc::tmem_wait_ld_regs(va);
+      const int mode = tile_mode(j);
+      auto run = [&](auto mode_c) {
+        uint32_t va[32], vb[32];
+        tc::tmem_ld32(tS, va);
+        tc::tmem_wait_ld_regs(va);
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; c += 2) {
-        tc::tmem_ld32(tS + (c + 1) * 32, vb);           // next chunk in flight
-        pass1_chunk(va, j * kBN + c * 32, fast);
-        tc::tmem_wait_ld_regs(vb);
-        if (c + 2 < kBN / 32) tc::tmem_ld32(tS + (c + 2) * 32, va);
-        pass1_chunk(vb, j * kBN + (c + 1) * 32, fast);
-        if (c + 2 < kBN / 32) tc::tmem_wait_ld_regs(va);
-      }
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars->sp_ready[t]);
+        for (int c = 0; c < kBN / 32; c += 2) {
+          tc::tmem_ld32(tS + (c + 1) * 32, vb);           // next chunk in flight
+          pass1_chunk(mode_c, va, j * kBN + c * 32);
+          tc::tmem_wait_ld_regs(vb);
+          if (c + 2 < kBN / 32) tc::tmem_ld32(tS + (c + 2) * 32, va);
+          else release_s();
+          pass1_chunk(mode_c, vb, j * kBN + (c + 1) * 32);
+          if (c + 2 < kBN / 32) tc::tmem_wait_ld_regs(va);
+        }
+      };
+      if (mode == kFast) run(IntC<kFast>{});
+      else if (mode == kLimited) run(IntC<kLimited>{});
+      else run(IntC<kGeneral>{});
     }
     if (!row_ok) m = 0.f;
     // pass 2: q = max(sigma(alpha (s - m))^tau, 1e-8) = 2^max(tau log2 sigma, ylo)
@@ -350,36 +392,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
       }
       return tc::ex2(fmaxf(y, ylo));
     };
-    auto pass2_chunk = [&](const uint32_t (&v)[32], int c, int key0, bool full) {
+    auto pass2_chunk = [&](auto mode_c, const uint32_t (&v)[32], int c, int key0) {
+      constexpr int kMode = decltype(mode_c)::value;
       uint32_t pk[16];
-      if (full) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float q0v = qval(fmaf(__uint_as_float(v[e]), sa2, -ma2));
-          const float q1v = qval(fmaf(__uint_as_float(v[e + 1]), sa2, -ma2));
-          l0 += q0v;
-          l1 += q1v;
-          pk[e >> 1] = tc::pack_bf16(q0v, q1v);
-        }
-      } else {
+      for (int e = 0; e < 32; e += 2) {
+        float qq[2];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float qq[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int key = key0 + e + u;
-            float qv = 0.f;
-            if (key < p.Lk) {
-              float sv = __uint_as_float(v[e + u]) * p.scale;
-              if (has_mask && row_ok) sv += fwd_mask_value(p, b, h, grow, key);
-              qv = qval((sv - m) * al2);
-            }
-            qq[u] = qv;
+        for (int u = 0; u < 2; ++u) {
+          const float raw = __uint_as_float(v[e + u]);
+          const int key = key0 + e + u;
+          if constexpr (kMode == kFast) {
+            qq[u] = qval(fmaf(raw, sa2, -ma2));
+          } else if constexpr (kMode == kLimited) {
+            // masked: ((s + finfo.min) - m) alpha log2(e), rounded as the reference
+            const float a2 = key < lim_c ? fmaf(raw, sa2, -ma2) : (raw * p.scale + kMaskMin - m) * al2;
+            const float qv = qval(a2);
+            qq[u] = key < p.Lk ? qv : 0.f;
+          } else {
+            // unmasked scores as in the fast path, masked ones as in the limited path
+            const float mv = row_ok ? fwd_mask_value(p, b, h, grow, key) : 0.f;
+            const float a2 = mv == 0.f ? fmaf(raw, sa2, -ma2) : (raw * p.scale + mv - m) * al2;
+            const float qv = qval(a2);
+            qq[u] = key < p.Lk ? qv : 0.f;
           }
-          l0 += qq[0];
-          l1 += qq[1];
-          pk[e >> 1] = tc::pack_bf16(qq[0], qq[1]);
         }
+        l0 += qq[0];
+        l1 += qq[1];
+        pk[e >> 1] = tc::pack_bf16(qq[0], qq[1]);
       }
       // 32 keys -> 4 x 16-byte chunks of the 128B-swizzled K-major P tile
       uint8_t* rowp = Pt + (c >> 1) * kTileBytes + r * 128;
@@ -391,22 +431,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
       }
     };
     for (int j = 0; j < nK && ok; ++j, ++i) {
+      // s_full also means the PV MMA of the previous step is done with P
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->s_full[t], i & 1, abort_flag, p.err, kErrTimeoutSoftmax));
       if (!ok) break;
       tc::tc_fence_after();
-      const bool full = (j + 1) * kBN <= p.Lk && !has_mask;
-      uint32_t va[32], vb[32];
-      tc::tmem_ld32(tS, va);
-      tc::tmem_wait_ld_regs(va);
+      const int mode = tile_mode(j);
+      auto run = [&](auto mode_c) {
+        uint32_t va[32], vb[32];
+        tc::tmem_ld32(tS, va);
+        tc::tmem_wait_ld_regs(va);
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; c += 2) {
-        tc::tmem_ld32(tS + (c + 1) * 32, vb);           // next chunk in flight
-        pass2_chunk(va, c, j * kBN + c * 32, full);
-        tc::tmem_wait_ld_regs(vb);
-        if (c + 2 < kBN / 32) tc::tmem_ld32(tS + (c + 2) * 32, va);
-        pass2_chunk(vb, c + 1, j * kBN + (c + 1) * 32, full);
-        if (c + 2 < kBN / 32) tc::tmem_wait_ld_regs(va);
-      }
+        for (int c = 0; c < kBN / 32; c += 2) {
+          tc::tmem_ld32(tS + (c + 1) * 32, vb);           // next chunk in flight
+          pass2_chunk(mode_c, va, c, j * kBN + c * 32);
+          tc::tmem_wait_ld_regs(vb);
+          if (c + 2 < kBN / 32) tc::tmem_ld32(tS + (c + 2) * 32, va);
+          else release_s();
+          pass2_chunk(mode_c, vb, c + 1, j * kBN + (c + 1) * 32);
+          if (c + 2 < kBN / 32) tc::tmem_wait_ld_regs(va);
+        }
+      };
+      if (mode == kFast) run(IntC<kFast>{});
+      else if (mode == kLimited) run(IntC<kLimited>{});
+      else run(IntC<kGeneral>{});
       tc::fence_async_smem();
       tc::tc_fence_before();
       __syncwarp();

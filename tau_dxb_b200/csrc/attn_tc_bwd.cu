@@ -124,6 +124,17 @@ __device__ __forceinline__ float bwd_mask_value(const BwdParams& p, int b, int h
   return mv;
 }
 
+template <bool B> struct BoolC { static constexpr bool value = B; };
+
+// Horner's rule on packed pairs, coefficients in increasing degree
+template <int N>
+__device__ __forceinline__ float2 horner2(const float2 (&c)[N], float2 x) {
+  float2 acc = c[N - 1];
+#pragma unroll
+  for (int i = N - 2; i >= 0; --i) acc = tc::fma2(acc, x, c[i]);
+  return acc;
+}
+
 template <int SIG>
 __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_constant__ BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -165,7 +176,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   const float tau = p.tau[h], alpha = p.alpha[h];
-
+  // Register split of the 80 x 768 launched: producer warpgroup (warps 0-3)
+  // and epilogue warpgroup 48 per thread, elementwise warps 96
+  // (48*128 + 48*128 + 96*512 = 61440). Each warpgroup's code is reached only
+  // through its own setmaxnreg, so the compiler allocates each to its limit.
+  static_assert(48 * 128 + 48 * 128 + 96 * 512 <= 80 * kThreads, "register split");
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 48;" ::: "memory");
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
@@ -289,7 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->qd_full[s]);
     }
-  } else if (warp >= 4 && warp < 8) {
+  }
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 48;" ::: "memory");
     // ---------------------------------------------------------------- dQ epilogue
     // One thread per query row; 32 TMEM columns in registers at a time.
     const int r = ((warp & 3) << 5) + lane;
@@ -398,7 +417,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       }
     }
     if (threadIdx.x == 128) tc::bulk_wait_group0();
-  } else if (warp >= 8) {
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 96;" ::: "memory");
     // ---------------------------------------------------------------- elementwise
     // Per score: a2 = log2(e) alpha (s scale - m), y = tau log2 sigma,
     // q = 2^max(y, ylo) (both clamps of the reference in one), P = q / Z,
@@ -419,9 +439,77 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     const float kmask = key_ok ? 1.f : 0.f;
     const float2 kmask2 = make_float2(kmask, kmask), sa2x2 = make_float2(sa2, sa2);
     const float2 taux2 = make_float2(tau, tau);
+    // polynomial coefficients as broadcast pairs: tau log2 sigma = tau a2 + cy(e)
+    // (tau folded in; minus for sigmoid's -H) and sigma'/sigma = cr(e)
+    float2 cy[TAU_POLY_DEG + 1], cr[TAU_POLY_DEG + 1];
+    {
+      const bool sg = SIG == TAU_DXB_SIGMA_SIGMOID;
+      const float g0[] = TAU_POLY_G_COEFFS, h0[] = TAU_POLY_H_COEFFS;
+      const float r0[] = TAU_POLY_R_COEFFS, s0[] = TAU_POLY_S_COEFFS;
+#pragma unroll
+      for (int u = 0; u <= TAU_POLY_DEG; ++u) {
+        const float yc = sg ? -tau * h0[u] : tau * g0[u], rc = sg ? s0[u] : r0[u];
+        cy[u] = make_float2(yc, yc);
+        cr[u] = make_float2(rc, rc);
+      }
+    }
     const bool tile_full = k0 + kT <= p.Lk;
     const bool has_mask = p.mask != nullptr || p.causal;
     float2 acc_tau = make_float2(0.f, 0.f), acc_alpha = make_float2(0.f, 0.f);
+    auto chunk_math = [&](auto masked_c, auto full_c, const uint32_t (&rr)[32], int i, int col0,
+                          uint32_t (&pp)[8], uint32_t (&pf)[8]) {
+      constexpr bool kMasked = decltype(masked_c)::value, kFull = decltype(full_c)::value;
+      const float* stc = stats + (i & 1) * 3 * kT;
+      float mv[kMasked ? 16 : 1];
+      if constexpr (kMasked) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int q = i * kT + col0 + e;
+          mv[e] = (key_ok && q < p.Lq) ? bwd_mask_value(p, b, h, q, key) : 0.f;
+        }
+      }
+#pragma unroll
+        for (int e4 = 0; e4 < 16; e4 += 4) {
+          const float4 mc4 = *reinterpret_cast<const float4*>(stc + col0 + e4);
+          const float4 rz4 = *reinterpret_cast<const float4*>(stc + kT + col0 + e4);
+          const float4 dq4 = *reinterpret_cast<const float4*>(stc + 2 * kT + col0 + e4);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {      // a pair of query columns per f32x2 lane pair
+            const int e = e4 + 2 * h2;
+            const float2 mc = h2 ? make_float2(mc4.z, mc4.w) : make_float2(mc4.x, mc4.y);
+            const float2 rz = h2 ? make_float2(rz4.z, rz4.w) : make_float2(rz4.x, rz4.y);
+            const float2 dq = h2 ? make_float2(dq4.z, dq4.w) : make_float2(dq4.x, dq4.y);
+            float2 a2 = tc::fma2(make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), sa2x2, mc);
+            if constexpr (kMasked) {
+              a2.x = fmaf(mv[e], al2, a2.x);
+              a2.y = fmaf(mv[e + 1], al2, a2.y);
+            }
+            float2 y, ratio;
+            if (SIG == TAU_DXB_SIGMA_SOFTPLUS || SIG == TAU_DXB_SIGMA_SIGMOID) {
+              const float2 ex = make_float2(tc::ex2(a2.x), tc::ex2(a2.y));
+              y = tc::fma2(taux2, a2, horner2(cy, ex));
+              ratio = horner2(cr, ex);
+            } else if (SIG == TAU_DXB_SIGMA_EXP) {
+              y = tc::mul2(taux2, a2);
+              ratio = make_float2(1.f, 1.f);
+            } else {
+              y = make_float2(ytau, ytau);
+              ratio = make_float2(1.f, 1.f);
+            }
+            float2 P = tc::mul2(make_float2(tc::ex2(fmaxf(y.x, ylo)), tc::ex2(fmaxf(y.y, ylo))), rz);
+            if constexpr (!kFull) P = tc::mul2(P, kmask2);
+            const float2 t = tc::mul2(P, tc::sub2(make_float2(__uint_as_float(rr[16 + e]),
+                                                              __uint_as_float(rr[17 + e])), dq));
+            acc_tau = tc::fma2(t, make_float2(fmaxf(y.x, ytau), fmaxf(y.y, ytau)), acc_tau);
+            // x = s - rowmax <= 0, so ratio * a2 <= 0: only the lower clip can act
+            const float2 ra = tc::mul2(ratio, a2);
+            acc_alpha = tc::fma2(t, make_float2(fmaxf(ra.x, -glim), fmaxf(ra.y, -glim)), acc_alpha);
+            const float2 F = tc::mul2(t, ratio);
+            pp[e >> 1] = tc::pack_bf16(P.x, P.y);
+            pf[e >> 1] = tc::pack_bf16(F.x, F.y);
+          }
+        }
+    };
     bool ok = true;
     for (int i = 0; i < nQ && ok; ++i) {
       const int s = i & 1;
@@ -430,7 +518,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc::tc_fence_after();
-      const float* st = stats + s * 3 * kT;
       uint8_t* DSt = smem + kOffDS + s * 2 * kTile + (grp >> 1) * kTile;   // this group's 64-query atom
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
@@ -445,52 +532,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           if (lane == 0) tc::mbar_arrive(&bars->s_free);
         }
         uint32_t pp[8], pf[8];
-#pragma unroll
-        for (int e4 = 0; e4 < 16; e4 += 4) {
-          const float4 mc4 = *reinterpret_cast<const float4*>(st + col0 + e4);
-          const float4 rz4 = *reinterpret_cast<const float4*>(st + kT + col0 + e4);
-          const float4 dq4 = *reinterpret_cast<const float4*>(st + 2 * kT + col0 + e4);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {      // a pair of query columns per f32x2 lane pair
-            const int e = e4 + 2 * h2;
-            const float2 mc = h2 ? make_float2(mc4.z, mc4.w) : make_float2(mc4.x, mc4.y);
-            const float2 rz = h2 ? make_float2(rz4.z, rz4.w) : make_float2(rz4.x, rz4.y);
-            const float2 dq = h2 ? make_float2(dq4.z, dq4.w) : make_float2(dq4.x, dq4.y);
-            float2 a2 = tc::fma2(make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), sa2x2, mc);
-            if (has_mask) {
-              const int q = i * kT + col0 + e;
-              if (key_ok && q < p.Lq) a2.x = fmaf(bwd_mask_value(p, b, h, q, key), al2, a2.x);
-              if (key_ok && q + 1 < p.Lq) a2.y = fmaf(bwd_mask_value(p, b, h, q + 1, key), al2, a2.y);
-            }
-            float2 y, ratio;
-            if (SIG == TAU_DXB_SIGMA_SOFTPLUS || SIG == TAU_DXB_SIGMA_SIGMOID) {
-              const float ex0 = tc::ex2(a2.x), ex1 = tc::ex2(a2.y);
-              if (SIG == TAU_DXB_SIGMA_SOFTPLUS) {
-                y = tc::mul2(taux2, tc::add2(a2, make_float2(poly::G(ex0), poly::G(ex1))));
-                ratio = make_float2(poly::R(ex0), poly::R(ex1));
-              } else {
-                y = tc::mul2(taux2, tc::sub2(a2, make_float2(poly::H(ex0), poly::H(ex1))));
-                ratio = make_float2(poly::S(ex0), poly::S(ex1));
-              }
-            } else if (SIG == TAU_DXB_SIGMA_EXP) {
-              y = tc::mul2(taux2, a2);
-              ratio = make_float2(1.f, 1.f);
-            } else {
-              y = make_float2(ytau, ytau);
-              ratio = make_float2(1.f, 1.f);
-            }
-            float2 P = tc::mul2(make_float2(tc::ex2(fmaxf(y.x, ylo)), tc::ex2(fmaxf(y.y, ylo))), rz);
-            if (!tile_full) P = tc::mul2(P, kmask2);
-            const float2 t = tc::mul2(P, tc::sub2(make_float2(__uint_as_float(rr[16 + e]),
-                                                              __uint_as_float(rr[17 + e])), dq));
-            acc_tau = tc::fma2(t, make_float2(fmaxf(y.x, ytau), fmaxf(y.y, ytau)), acc_tau);
-            // x = s - rowmax <= 0, so ratio * a2 <= 0: only the lower clip can act
-            const float2 ra = tc::mul2(ratio, a2);
-            acc_alpha = tc::fma2(t, make_float2(fmaxf(ra.x, -glim), fmaxf(ra.y, -glim)), acc_alpha);
-            const float2 F = tc::mul2(t, ratio);
-            pp[e >> 1] = tc::pack_bf16(P.x, P.y);
-            pf[e >> 1] = tc::pack_bf16(F.x, F.y);
-          }
+        // branch-free bodies (mask / partial key tile decided per chunk) so the
+        // scheduler can interleave the eight column pairs
+        if (has_mask) {
+          if (tile_full) chunk_math(BoolC<true>{}, BoolC<true>{}, rr, i, col0, pp, pf);
+          else chunk_math(BoolC<true>{}, BoolC<false>{}, rr, i, col0, pp, pf);
+        } else {
+          if (tile_full) chunk_math(BoolC<false>{}, BoolC<true>{}, rr, i, col0, pp, pf);
+          else chunk_math(BoolC<false>{}, BoolC<false>{}, rr, i, col0, pp, pf);
         }
         if (c == 0) {
           // P^T in TMEM is free once the previous tile's dV MMA is done, the dS^T
