@@ -70,6 +70,122 @@ __global__ void write_dk_kernel(const AttnProblem p) {
   }
 }
 
+// ---- vectorized forms for bf16, D = 64, unit d-stride, 16-byte aligned rows
+// (the tensor-core path's layouts). Eight threads cover one 64-element row,
+// 16 bytes of bf16 (32 bytes of fp32) each.
+constexpr int kVecD = 64;
+
+__device__ __forceinline__ void bf16x8_to_f32(uint4 w, float (&f)[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    f[2 * k] = __uint_as_float(u[k] << 16);
+    f[2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ uint4 f32x8_to_bf16(const float (&f)[8]) {
+  uint4 w;
+  uint32_t* u = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __nv_bfloat162 b2 = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+    u[k] = *reinterpret_cast<const uint32_t*>(&b2);
+  }
+  return w;
+}
+__device__ __forceinline__ const uint4* row_ptr(const void* base, const int64_t* s, int b, int h, int l,
+                                                int part) {
+  return reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(base) + b * s[0] + h * s[1] +
+                                        static_cast<int64_t>(l) * s[2]) + part;
+}
+
+// Drow = rowsum(dO * O); also zeroes the dQ accumulator row and rowsum(F).
+__global__ void prep_vec_kernel(const AttnProblem p) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = t >> 3;
+  const int part = static_cast<int>(t & 7);
+  const int64_t nrows = static_cast<int64_t>(p.B) * p.H * p.Lq;
+  if (row >= nrows) return;     // whole groups of 8 lanes leave together
+  const int bh = static_cast<int>(row / p.Lq), i = static_cast<int>(row - static_cast<int64_t>(bh) * p.Lq);
+  const int b = bh / p.H, h = bh - b * p.H;
+  float g[8], o[8];
+  bf16x8_to_f32(__ldg(row_ptr(p.dout, p.dos, b, h, i, part)), g);
+  bf16x8_to_f32(__ldg(row_ptr(p.o, p.os, b, h, i, part)), o);
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc = fmaf(g[k], o[k], acc);
+  const unsigned grp = 0xffu << (threadIdx.x & 24);   // this row's 8 lanes
+  acc += __shfl_xor_sync(grp, acc, 4);
+  acc += __shfl_xor_sync(grp, acc, 2);
+  acc += __shfl_xor_sync(grp, acc, 1);
+  float4* dq = reinterpret_cast<float4*>(p.ws_dq + row * kVecD) + 2 * part;
+  dq[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  dq[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (part == 0) {
+    p.ws_drow[row] = acc;
+    p.ws_rowf[row] = 0.f;
+  }
+  if (t < p.H) {
+    p.dtau[t] = 0.f;
+    p.dalpha[t] = 0.f;
+  }
+}
+
+// dQ_i = scale (acc_i - rowF_i K[amax_i]) as bf16; dK_acc[amax_i] -= rowF_i Q_i.
+__global__ void fix_dq_vec_kernel(const AttnProblem p) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = t >> 3;
+  const int part = static_cast<int>(t & 7);
+  const int64_t nrows = static_cast<int64_t>(p.B) * p.H * p.Lq;
+  if (row >= nrows) return;
+  const int bh = static_cast<int>(row / p.Lq), i = static_cast<int>(row - static_cast<int64_t>(bh) * p.Lq);
+  const int b = bh / p.H, h = bh - b * p.H;
+  const float f = p.ws_rowf[row];
+  const int a = p.row_argmax[row];
+  const float4* acc = reinterpret_cast<const float4*>(p.ws_dq + row * kVecD) + 2 * part;
+  const float4 a0 = acc[0], a1 = acc[1];
+  float g[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  if (a >= 0 && a < p.Lk) {
+    float kv[8], qv[8];
+    bf16x8_to_f32(__ldg(row_ptr(p.k, p.ks, b, h, a, part)), kv);
+    bf16x8_to_f32(__ldg(row_ptr(p.q, p.qs, b, h, i, part)), qv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) g[k] = fmaf(-f, kv[k], g[k]);
+    float4* dk = reinterpret_cast<float4*>(p.ws_dk + (static_cast<int64_t>(bh) * p.Lk + a) * kVecD) + 2 * part;
+    atomicAdd(dk, make_float4(-f * qv[0], -f * qv[1], -f * qv[2], -f * qv[3]));
+    atomicAdd(dk + 1, make_float4(-f * qv[4], -f * qv[5], -f * qv[6], -f * qv[7]));
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) g[k] *= p.scale;
+  *reinterpret_cast<uint4*>(const_cast<uint4*>(row_ptr(p.dq, p.dqs, b, h, i, part))) = f32x8_to_bf16(g);
+}
+
+__global__ void write_dk_vec_kernel(const AttnProblem p) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = t >> 3;
+  const int part = static_cast<int>(t & 7);
+  const int64_t nrows = static_cast<int64_t>(p.B) * p.H * p.Lk;
+  if (row >= nrows) return;
+  const int bh = static_cast<int>(row / p.Lk), j = static_cast<int>(row - static_cast<int64_t>(bh) * p.Lk);
+  const int b = bh / p.H, h = bh - b * p.H;
+  const float4* acc = reinterpret_cast<const float4*>(p.ws_dk + row * kVecD) + 2 * part;
+  const float4 a0 = acc[0], a1 = acc[1];
+  const float g[8] = {a0.x * p.scale, a0.y * p.scale, a0.z * p.scale, a0.w * p.scale,
+                      a1.x * p.scale, a1.y * p.scale, a1.z * p.scale, a1.w * p.scale};
+  *reinterpret_cast<uint4*>(const_cast<uint4*>(row_ptr(p.dk, p.dks, b, h, j, part))) = f32x8_to_bf16(g);
+}
+
+bool vec_layout_ok(const void* ptr, const int64_t s[4]) {
+  return s[3] == 1 && reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && s[0] % 8 == 0 && s[1] % 8 == 0 &&
+         s[2] % 8 == 0;
+}
+bool vec_ok(const AttnProblem& p) {
+  return p.dtype == TAU_DXB_BF16 && p.D == kVecD && vec_layout_ok(p.q, p.qs) && vec_layout_ok(p.k, p.ks) &&
+         vec_layout_ok(p.o, p.os) && vec_layout_ok(p.dout, p.dos) && vec_layout_ok(p.dq, p.dqs) &&
+         vec_layout_ok(p.dk, p.dks) && static_cast<int64_t>(p.B) * p.H * (p.Lq > p.Lk ? p.Lq : p.Lk) < (1ll << 31);
+}
+unsigned vec_blocks(int64_t rows) { return static_cast<unsigned>((rows * 8 + 255) / 256); }
+
 template <typename T>
 int prologue(const AttnProblem& p, cudaStream_t st) {
   const int64_t nrows = static_cast<int64_t>(p.B) * p.H * p.Lq;
@@ -112,6 +228,11 @@ WorkspaceLayout workspace_layout(int64_t B, int64_t H, int64_t Lq, int64_t Lk, i
 }
 
 int attn_bwd_prologue(const AttnProblem& p, cudaStream_t st) {
+  const int64_t nrows = static_cast<int64_t>(p.B) * p.H * p.Lq;
+  if (vec_ok(p) && nrows >= p.H) {
+    prep_vec_kernel<<<vec_blocks(nrows), 256, 0, st>>>(p);
+    return check_launch("prep_vec_kernel");
+  }
   const WorkspaceLayout w = workspace_layout(p.B, p.H, p.Lq, p.Lk, p.D);
   // dQ accumulator, rowsum(F) and the per-head sums start at zero.
   TDX_CUDA(cudaMemsetAsync(p.ws_dq, 0, w.dk - w.dq, st));
@@ -126,6 +247,19 @@ int attn_bwd_prologue(const AttnProblem& p, cudaStream_t st) {
 }
 
 int attn_bwd_epilogue(const AttnProblem& p, cudaStream_t st) {
+  if (vec_ok(p)) {
+    const int64_t nq = static_cast<int64_t>(p.B) * p.H * p.Lq, nk = static_cast<int64_t>(p.B) * p.H * p.Lk;
+    if (nq > 0) {
+      fix_dq_vec_kernel<<<vec_blocks(nq), 256, 0, st>>>(p);
+      const int rc = check_launch("fix_dq_vec_kernel");
+      if (rc) return rc;
+    }
+    if (nk > 0) {
+      write_dk_vec_kernel<<<vec_blocks(nk), 256, 0, st>>>(p);
+      return check_launch("write_dk_vec_kernel");
+    }
+    return TAU_DXB_OK;
+  }
   switch (p.dtype) {
     case TAU_DXB_F32: return epilogue<float>(p, st);
     case TAU_DXB_BF16: return epilogue<__nv_bfloat16>(p, st);
