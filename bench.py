@@ -50,6 +50,23 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+# DRAM bytes per launch (read + write) of the main kernels at the encoder_self
+# workload (B=16), from one ncu capture each; traffic grows with B.
+BWD_MAIN_TRAFFIC = 360.6e6
+FWD_TRAFFIC = 131.5e6
+
+
+def sfu_floor(c, ms, clk, sms):
+    """Second roofline: the special-function (ex2) pipe. The forward and the
+    backward each spend 2 exp2 per score for softplus/sigmoid; the pipe does 16
+    per clock per SM."""
+    mhz = clk.get("sm_mhz") or 1965.0
+    n = 4.0 * c["B"] * c["H"] * c["Lq"] * c["Lk"]
+    floor_ms = n / (16.0 * sms * mhz * 1e6) * 1e3
+    return {"ex2_per_score_fwd_bwd": 4, "floor_ms": round(floor_ms, 4), "measured_ms": round(ms, 4),
+            "frac": round(floor_ms / ms, 4), "sm_mhz": mhz}
+
+
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
@@ -436,6 +453,7 @@ def run_ours(args, rank, world, local_rank):
         fwd_ach = fwd_fl / (fwd_ms * 1e-3) / 1e12
         dom_is_bwd = bwd_ms >= fwd_ms
         ach = bwd_ach if dom_is_bwd else fwd_ach
+        clk_summary = clk.summary()
         result = {
             "metric": "tau-opus attention fwd+bwd throughput (encoder_self softplus)",
             "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
@@ -447,12 +465,18 @@ def run_ours(args, rank, world, local_rank):
                        "flops_per_step": flops, "l2": "inputs larger than L2 (working set ~440 MB per step)",
                        "parallelism": f"replicas x{world} (independent batches, no collective)"},
             "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
-            "roofline": {"bound": "tensor", "kernel": "tau_attn_bwd (all launches)" if dom_is_bwd
-                         else "tau_attn_fwd", "achieved": round(ach, 2), "peak": bf16,
-                         "unit": "TFLOP/s", "frac": round(ach / bf16, 4), "traffic": None,
+            "roofline": {"bound": "tensor", "kernel": "tau_attn_bwd call (prep + attn_bwd_tc_kernel + "
+                         "fix_dq + write_dk)" if dom_is_bwd else "tau_attn_fwd call (attn_fwd_tc_kernel)",
+                         "achieved": round(ach, 2), "peak": bf16,
+                         "unit": "TFLOP/s", "frac": round(ach / bf16, 4),
+                         "traffic": BWD_MAIN_TRAFFIC if dom_is_bwd else FWD_TRAFFIC,
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of the main kernel per "
+                                         "launch, one ncu capture of this workload",
                          "peak_kind": peak_kind + " burst bf16",
-                         "fwd_achieved": round(fwd_ach, 2), "bwd_achieved": round(bwd_ach, 2)},
-            "clocks": clk.summary(),
+                         "fwd_achieved": round(fwd_ach, 2), "bwd_achieved": round(bwd_ach, 2),
+                         "sfu": sfu_floor(c, fwd_ms + bwd_ms, clk_summary,
+                                                  torch.cuda.get_device_properties(device).multi_processor_count)},
+            "clocks": clk_summary,
             "gpu_launches": args.steps * r_launches_per_step(),
         }
         if e2e:
