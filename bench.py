@@ -586,6 +586,8 @@ def main():
     ap.add_argument("--no-train", action="store_true", help="skip the Whisper train-step sub-benchmark")
     ap.add_argument("--profile-batch", type=int, default=0,
                     help="headline kernels only, at this batch size (small cases for ncu captures)")
+    ap.add_argument("--wta-only", action="store_true",
+                    help="only the WTA sub-benchmark (JSON of its results; for ncu captures)")
     args = ap.parse_args()
     if args.profile_batch:
         args.quick = args.no_e2e = args.no_cpu = args.no_train = True
@@ -609,6 +611,14 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+    if args.wta_only:
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        if rank == 0:
+            print(json.dumps({"wta": wta_sub_bench(torch, device)}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     try:
         res = run_ours(args, rank, world, local_rank)
         if rank == 0 and res is not None:

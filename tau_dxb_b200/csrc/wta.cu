@@ -1,15 +1,17 @@
 // WTA top-k sparsity kernels (K4 forward / K5 backward) for sm_100a.
 //
-// Forward: one warp per row. A bf16/f16 row of d = 256*CH elements is read
-// once with 128-bit loads into registers (CH*4 words per lane), turned into
-// order-preserving 16-bit keys, and the k-th largest key is found by a
-// two-pass MSB radix select (8-bit digits). Every lane counts its own keys in
-// a private column of a [257 bins][32 lanes] u8 histogram in shared memory
-// (no atomics, no cross-lane contention); a digit pass ends with one warp
-// reduction that locates the digit holding the k-th largest key. The mask is
-// then written as bits (1/8 byte per element), y = keep ? x : 0 as bf16, and
+// Forward, fast path (bf16/f16 rows of d = 256*CH, 16-byte aligned): one warp
+// per row, read once with 128-bit loads into registers (CH*4 words per lane).
+// The k-th largest value is found by a search over the ordered 16-bit value
+// space whose probe, count(x >= v), is one packed bf16x2/f16x2 compare per two
+// elements plus a warp reduction -- registers only, no shared memory. Each
+// warp starts its search at the threshold of the row it did before. The mask
+// is written as bits (1/8 byte per element), y = keep ? x : 0 as bf16, and
 // optionally per-column win counts. HBM traffic per element: 2 B read, 2 B
 // written (y), 1/8 B mask -- nothing else touches DRAM.
+// Generic path (fp32, other widths, unaligned rows): two-pass MSB radix
+// select (8-bit digits) over order-preserving keys with per-lane shared-memory
+// counters.
 //
 // Semantics (reference):
 //   threshold -- keep = x >= k-th largest value (echo/triton_wta.py:81-83,46-47;
@@ -34,10 +36,6 @@ constexpr uint32_t kFull = 0xffffffffu;
 __device__ __forceinline__ uint32_t keys16(uint32_t w) {
   const uint32_t s = (w >> 15) & 0x00010001u;          // sign of each half
   return w ^ ((s * 0x7FFFu) | 0x80008000u);
-}
-__device__ __forceinline__ uint32_t unkeys16(uint32_t kw) {
-  const uint32_t s = ((~kw) >> 15) & 0x00010001u;      // 1 where x was negative
-  return kw ^ ((s * 0x7FFFu) | 0x80008000u);
 }
 __device__ __forceinline__ uint32_t key32(uint32_t w) {
   return w ^ ((w & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
@@ -113,88 +111,115 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
 }
 
 // ---------------------------------------------------------------------------
-// Fast path: 16-bit elements, d = 256 * CH, rows 16-byte aligned.
+// Fast path: 16-bit floats (bf16 / f16), d = 256 * CH, rows 16-byte aligned.
 //
-// Counters: per warp a [257 bins][16 words] u32 array; lane l owns the 16-bit
-// half (l & 1) of word (l >> 1) in every bin row. Updates are fire-and-forget
-// `red.shared.add` (no load-add-store dependency chain through shared memory);
-// only the two lanes sharing a word can collide on one address.
+// One warp per row, the row held in registers (CH x 16 bytes per lane). The
+// k-th largest value t is found by a search over the ordered 16-bit value
+// space, with no shared memory: count_ge(v) = #{x >= v} costs one packed
+// compare per two elements (set.ge.u32.{bf16x2,f16x2} gives 0xFFFF per true
+// half) and one subtraction into a register accumulator, then one warp
+// reduction. The search starts at the threshold of the row this warp did
+// before (rows of one activation tensor are alike): it gallops away from it
+// until the answer is bracketed, then bisects; the first row of a warp
+// bisects the whole range.
+//
+// The compares are float compares, as in the reference: +0 == -0. The search
+// counts NaN as larger than everything (set.geu), as torch.topk / kthvalue
+// order it, so with n NaN in a row t is the (k - n)-th largest non-NaN value;
+// the mask compare x >= t is ordered, so NaN is never kept, and a row with
+// n >= k keeps nothing (the reference's threshold is then NaN).
 
-__device__ __forceinline__ void red_shared_add(uint32_t addr, uint32_t v) {
-  asm volatile("red.shared.add.u32 [%0], %1;" :: "r"(addr), "r"(v) : "memory");
+// Bit pattern of the 16-bit float whose order-preserving key (keys16) is `key`.
+__device__ __forceinline__ uint32_t key_to_bits16(uint32_t key) {
+  return key ^ ((key & 0x8000u) ? 0x8000u : 0xFFFFu);
 }
 
-// Find the digit bin holding the k-th largest key from u16-pair counters.
-// Lane l owns bins l + 32*j; it sums the 16 words of each of its bins (4
-// staggered 16-byte loads, conflict-free) and zeroes them.
-__device__ __forceinline__ void select_bin_pairs(uint32_t* hist, int lane, int k, int& bstar,
-                                                 int& above_out) {
-  uint32_t cnt[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    uint4* row = reinterpret_cast<uint4*>(hist + (lane + 32 * j) * 16);
-    uint32_t acc = 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int c = (q + (lane >> 1)) & 3;
-      const uint4 a = row[c];
-      acc += a.x + a.y + a.z + a.w;          // two 16-bit fields, each <= d
-      row[c] = make_uint4(0, 0, 0, 0);
-    }
-    cnt[j] = (acc & 0xFFFFu) + (acc >> 16);
-  }
-  int above = 0, jstar = 0;
-  bool found = false;
-#pragma unroll
-  for (int j = 7; j >= 0; --j) {
-    const int g = static_cast<int>(__reduce_add_sync(kFull, cnt[j]));
-    if (!found) {
-      if (above + g >= k) { jstar = j; found = true; }
-      else above += g;
-    }
-  }
-  uint32_t c = cnt[0];
-#pragma unroll
-  for (int j = 1; j < 8; ++j) if (j == jstar) c = cnt[j];
-  uint32_t s = c;                                // inclusive suffix sum over lanes
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const uint32_t t = __shfl_down_sync(kFull, s, off);
-    if (lane + off < 32) s += t;
-  }
-  const uint32_t S = s + static_cast<uint32_t>(above);
-  const uint32_t ge = __ballot_sync(kFull, S >= static_cast<uint32_t>(k));
-  const int lstar = 31 - __clz(ge);
-  const uint32_t S_l = __shfl_sync(kFull, S, lstar);
-  const uint32_t c_l = __shfl_sync(kFull, c, lstar);
-  bstar = 32 * jstar + lstar;
-  above_out = static_cast<int>(S_l - c_l);
+template <bool BF>
+__device__ __forceinline__ uint32_t cmp_ge2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (BF) asm("set.ge.u32.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("set.ge.u32.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// x >= v or unordered: NaN counts as larger than every value (torch's order)
+template <bool BF>
+__device__ __forceinline__ uint32_t cmp_geu2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (BF) asm("set.geu.u32.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("set.geu.u32.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <bool BF>
+__device__ __forceinline__ uint32_t cmp_gt2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (BF) asm("set.gt.u32.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("set.gt.u32.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <bool BF>
+__device__ __forceinline__ uint32_t cmp_eq2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (BF) asm("set.eq.u32.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("set.eq.u32.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// acc - m as an integer multiply-add by a register holding -1 (neg1, not a
+// compile-time constant, so it stays a multiply-add): the packed compares
+// occupy the ALU pipe, the accumulation goes to the FMA pipe.
+__device__ __forceinline__ uint32_t sub_mad(uint32_t acc, uint32_t m, uint32_t neg1) {
+  uint32_t r;
+  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(m), "r"(neg1), "r"(acc));
+  return r;
+}
+
+// Sum of packed compare masks: subtracting a mask m = 0xFFFF*l + 0xFFFF0000*h
+// adds l - 65536*(l - h) (mod 2^32), so a sum S over words (and lanes) holds
+// L = S mod 65536 true low halves and (S - L) / 65536 = H - L; exact while
+// L < 65536 and |H - L| < 32768 (d <= 4096 here).
+__device__ __forceinline__ int decode_mask_sum(uint32_t s) {
+  const uint32_t lo = s & 0xFFFFu;
+  return static_cast<int>(2u * lo) + (static_cast<int>(s - lo) >> 16);
+}
+
+// Mask byte of 8 consecutive elements from the 4 packed masks of one lane's
+// 16-byte chunk: bit 2i <- low half of m_i, bit 2i+1 <- high half.
+__device__ __forceinline__ uint32_t mask_byte(uint32_t m0, uint32_t m1, uint32_t m2, uint32_t m3) {
+  const uint32_t t = (m0 & 0x00010001u) | ((m1 & 0x00010001u) << 2) | ((m2 & 0x00010001u) << 4) |
+                     ((m3 & 0x00010001u) << 6);
+  return (t | (t >> 15)) & 0xFFu;
 }
 
 constexpr int kFastWarps = 4;                    // rows in flight per block
-constexpr int kPairHistBytes = kBins * 64;       // [257][16] u32 per warp
+constexpr uint32_t kGallopMax = 64;
 
-template <int CH, bool EXACT, bool WRITE_Y, bool HIST>
-__global__ void __launch_bounds__(kFastWarps * 32, 3)
+template <bool B> struct BoolC { static constexpr bool value = B; };
+
+// Blocks per SM the register budget is sized for: two rows (this one and the
+// prefetched next) take 8*CH registers per thread.
+template <int CH, bool HIST>
+constexpr int fwd16_min_blocks() { return CH > 12 ? 2 : (CH == 12 && HIST ? 3 : 4); }
+
+template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST>
+__global__ void __launch_bounds__(kFastWarps * 32, fwd16_min_blocks<CH, HIST>())
 wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_stride,
                  int k_host, const int32_t* __restrict__ k_dev,
                  uint16_t* __restrict__ y, uint8_t* __restrict__ bitmask,
                  int32_t* __restrict__ win) {
   constexpr int D = 256 * CH;
+  // key range of the non-NaN values: [-inf, +inf]
+  constexpr uint32_t kNeg = BF ? 0x007Fu : 0x03FFu, kPos = BF ? 0xFF80u : 0xFC00u;
   extern __shared__ __align__(16) uint8_t smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + warp * kPairHistBytes);
-  int32_t* shist = reinterpret_cast<int32_t*>(smem + kFastWarps * kPairHistBytes);
-  for (int i = lane; i < kPairHistBytes / 16; i += 32)
-    reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
-  if (HIST)
+  int32_t* shist = reinterpret_cast<int32_t*>(smem);
+  if (HIST) {
     for (int i = threadIdx.x; i < D; i += blockDim.x) shist[i] = 0;
-  __syncthreads();
+    __syncthreads();
+  }
   int k = k_dev ? *k_dev : k_host;
   k = max(1, min(D, k));
-  // this lane's counter: word (lane >> 1) of a bin row, 16-bit half (lane & 1)
-  const uint32_t hbase = static_cast<uint32_t>(__cvta_generic_to_shared(hist)) + (lane >> 1) * 4;
-  const uint32_t inc = 1u << ((lane & 1) * 16);
+  // -1 for every valid launch (row_stride >= 0), unknown to the compiler
+  const uint32_t neg1 = ~static_cast<uint32_t>(row_stride >> 63);
 
   const int64_t stride_rows = static_cast<int64_t>(gridDim.x) * kFastWarps;
   int64_t row = static_cast<int64_t>(blockIdx.x) * kFastWarps + warp;
@@ -204,13 +229,15 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
 #pragma unroll
     for (int c = 0; c < CH; ++c) nxt[c] = __ldcs(src + c * 32 + lane);
   }
+  // warp-uniform search state: the previous row's threshold key and how far
+  // it moved from the row before; galloping pays while that distance is small
+  // (about 2 log2(distance) + 2 probes against 16 for a full bisection)
+  bool have_prev = false;
+  uint32_t t_prev = 0, dist_prev = 0;
   for (; row < n_rows; row += stride_rows) {
-    uint32_t kw[CH][4];
+    uint4 w[CH];
 #pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      kw[c][0] = keys16(nxt[c].x); kw[c][1] = keys16(nxt[c].y);
-      kw[c][2] = keys16(nxt[c].z); kw[c][3] = keys16(nxt[c].w);
-    }
+    for (int c = 0; c < CH; ++c) w[c] = nxt[c];
     // prefetch the next row while this one is selected
     const int64_t nrow = row + stride_rows;
     if (nrow < n_rows) {
@@ -218,87 +245,114 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
 #pragma unroll
       for (int c = 0; c < CH; ++c) nxt[c] = __ldcs(src + c * 32 + lane);
     }
-    // pass 1: high byte of every key
+    // #{x >= v}, NaN included when UNORD (NaN sorts above +inf)
+    auto count_ge = [&](uint32_t key, auto unord) -> int {
+      const uint32_t b = key_to_bits16(key);
+      const uint32_t v2 = b | (b << 16);
+      uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
 #pragma unroll
-    for (int c = 0; c < CH; ++c)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t w = kw[c][i];
-        red_shared_add(hbase + __byte_perm(w, 0, 0x4441) * 64, inc);
-        red_shared_add(hbase + (w >> 24) * 64, inc);
+      for (int c = 0; c < CH; ++c) {
+        if constexpr (decltype(unord)::value) {
+          a0 = sub_mad(a0, cmp_geu2<BF>(w[c].x, v2), neg1);
+          a1 = sub_mad(a1, cmp_geu2<BF>(w[c].y, v2), neg1);
+          a2 = sub_mad(a2, cmp_geu2<BF>(w[c].z, v2), neg1);
+          a3 = sub_mad(a3, cmp_geu2<BF>(w[c].w, v2), neg1);
+        } else {
+          a0 = sub_mad(a0, cmp_ge2<BF>(w[c].x, v2), neg1);
+          a1 = sub_mad(a1, cmp_ge2<BF>(w[c].y, v2), neg1);
+          a2 = sub_mad(a2, cmp_ge2<BF>(w[c].z, v2), neg1);
+          a3 = sub_mad(a3, cmp_ge2<BF>(w[c].w, v2), neg1);
+        }
       }
-    __syncwarp();
-    int b1, above1;
-    select_bin_pairs(hist, lane, k, b1, above1);
-    __syncwarp();
-    // pass 2: low byte of keys whose high byte is b1; others go to bin 256
-    const uint32_t hb2 = (static_cast<uint32_t>(b1) << 8) | (static_cast<uint32_t>(b1) << 24);
-#pragma unroll
-    for (int c = 0; c < CH; ++c)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t xw = kw[c][i] ^ hb2;            // matching keys -> high byte 0
-        red_shared_add(hbase + min(xw & 0xFFFFu, 256u) * 64, inc);
-        red_shared_add(hbase + min(xw >> 16, 256u) * 64, inc);
+      return decode_mask_sum(__reduce_add_sync(kFull, (a0 + a1) + (a2 + a3)));
+    };
+    // The largest t with #{x >= t} + #NaN >= k is the (k - #NaN)-th largest
+    // non-NaN value. Invariant: count(lo) >= k > count(hi) = c_hi, with the
+    // sentinel hi = kPos + 1 ("above +inf"); count(kNeg) = d >= k.
+    uint32_t lo = kNeg, hi = kPos + 1;
+    const bool gallop = have_prev && dist_prev <= kGallopMax;
+    if (gallop) {
+      const int c = count_ge(t_prev, BoolC<true>{});
+      if (c >= k) {
+        lo = t_prev;
+        for (uint32_t step = 1; lo + step < hi; step <<= 1) {
+          const uint32_t p = lo + step;
+          if (count_ge(p, BoolC<true>{}) >= k) {
+            lo = p;
+          } else {
+            hi = p;
+            break;
+          }
+        }
+      } else {
+        hi = t_prev;
+        for (uint32_t step = 1; hi - kNeg > step; step <<= 1) {
+          const uint32_t p = hi - step;
+          if (count_ge(p, BoolC<true>{}) >= k) {
+            lo = p;
+            break;
+          }
+          hi = p;
+        }
       }
-    __syncwarp();
-    int b2, above2;
-    select_bin_pairs(hist, lane, k - above1, b2, above2);
-    __syncwarp();
-    const uint32_t t = (static_cast<uint32_t>(b1) << 8) | static_cast<uint32_t>(b2);
-    uint32_t tlo = t, thi = t;
-    if (t == 0x8000u || t == 0x7FFFu) { tlo = 0x7FFFu; thi = 0x8000u; }   // +0 == -0
-
-    int need = 0, rank_base = 0;
-    if (EXACT) {
-      int gt = 0;
-#pragma unroll
-      for (int c = 0; c < CH; ++c)
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          gt += ((kw[c][i] & 0xFFFFu) > thi) + ((kw[c][i] >> 16) > thi);
-      need = k - static_cast<int>(__reduce_add_sync(kFull, static_cast<uint32_t>(gt)));
     }
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (count_ge(mid, BoolC<true>{}) >= k) lo = mid;
+      else hi = mid;
+    }
+    uint32_t t = lo;
+    bool none = false;
+    int c_gt = 0;                  // #{non-NaN x > t}
+    if (t == kPos) {
+      // threshold +inf, or #NaN >= k: then the reference's threshold is NaN
+      // and nothing is kept
+      const int n_nan = count_ge(kPos, BoolC<true>{}) - count_ge(kPos, BoolC<false>{});
+      none = n_nan >= k;
+    } else if (EXACT) {
+      c_gt = count_ge(t + 1, BoolC<false>{});
+    }
+    dist_prev = have_prev ? (t > t_prev ? t - t_prev : t_prev - t) : 0u;
+    t_prev = t;
+    have_prev = true;
+    const uint32_t tb = key_to_bits16(t);
+    const uint32_t t2 = tb | (tb << 16);
+    const int need = k - c_gt;     // exact_k: ties at t kept in index order
+    int rank_base = 0;
     uint8_t* mrow = bitmask + row * (D / 8);
     uint4* yrow = WRITE_Y ? reinterpret_cast<uint4*>(y + row * static_cast<int64_t>(D)) : nullptr;
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      uint32_t bits = 0;
+      const uint32_t wv[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
+      uint32_t m[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t lo = kw[c][i] & 0xFFFFu, hi = kw[c][i] >> 16;
-        if (EXACT) {
-          bits |= static_cast<uint32_t>(lo > thi) << (2 * i);
-          bits |= static_cast<uint32_t>(hi > thi) << (2 * i + 1);
-        } else {
-          bits |= static_cast<uint32_t>(lo >= tlo) << (2 * i);
-          bits |= static_cast<uint32_t>(hi >= tlo) << (2 * i + 1);
-        }
-      }
+      for (int i = 0; i < 4; ++i) m[i] = none ? 0u : (EXACT ? cmp_gt2<BF>(wv[i], t2) : cmp_ge2<BF>(wv[i], t2));
+      uint32_t bits = mask_byte(m[0], m[1], m[2], m[3]);
       if (EXACT) {
-        uint32_t tie = 0;
+        uint32_t e[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t lo = kw[c][i] & 0xFFFFu, hi = kw[c][i] >> 16;
-          tie |= static_cast<uint32_t>(lo >= tlo && lo <= thi) << (2 * i);
-          tie |= static_cast<uint32_t>(hi >= tlo && hi <= thi) << (2 * i + 1);
-        }
+        for (int i = 0; i < 4; ++i) e[i] = none ? 0u : cmp_eq2<BF>(wv[i], t2);
+        const uint32_t tie = mask_byte(e[0], e[1], e[2], e[3]);
         int total;
         int r = rank_base + warp_excl_scan(__popc(tie), lane, total);
         rank_base += total;
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if ((tie >> e) & 1u) { if (r < need) bits |= 1u << e; ++r; }
+        for (int b = 0; b < 8; ++b)
+          if ((tie >> b) & 1u) { if (r < need) bits |= 1u << b; ++r; }
       }
       mrow[c * 32 + lane] = static_cast<uint8_t>(bits);
       if (WRITE_Y) {
         uint32_t o[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          uint32_t sel = (((bits >> (2 * i)) & 1u) ? 0x0000FFFFu : 0u) |
-                         (((bits >> (2 * i + 1)) & 1u) ? 0xFFFF0000u : 0u);
-          if (EXACT) sel |= 0x80008000u;   // x * 0 keeps the sign
-          o[i] = unkeys16(kw[c][i]) & sel;
+          if (EXACT) {
+            // y = x * keep: a dropped value keeps only its sign
+            const uint32_t sel = (((bits >> (2 * i)) & 1u) ? 0x0000FFFFu : 0u) |
+                                 (((bits >> (2 * i + 1)) & 1u) ? 0xFFFF0000u : 0u) | 0x80008000u;
+            o[i] = wv[i] & sel;
+          } else {
+            o[i] = wv[i] & m[i];    // y = where(keep, x, +0)
+          }
         }
         __stcs(yrow + c * 32 + lane, make_uint4(o[0], o[1], o[2], o[3]));
       }
@@ -319,17 +373,24 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
 
 // ---------------------------------------------------------------------------
 // Generic path: any d < 65536, any supported dtype, any row stride. One warp
-// per row; the row is re-read (L1/L2) for every digit pass.
-template <typename T>
-__device__ __forceinline__ uint32_t load_key(const T* p);
-template <> __device__ __forceinline__ uint32_t load_key<uint16_t>(const uint16_t* p) {
-  return keys16(static_cast<uint32_t>(*p)) & 0xFFFFu;
+// per row; the row is re-read (L1/L2) for every digit pass. NaN gets key 0,
+// below every other key, and the select runs on k - #NaN, so NaN is handled as
+// on the fast path (never kept; t is the (k - #NaN)-th largest non-NaN value).
+// FMT: 0 fp32, 1 bf16, 2 f16.
+template <int FMT>
+__device__ __forceinline__ bool is_nan_bits(uint32_t b) {
+  if (FMT == 0) return (b & 0x7FFFFFFFu) > 0x7F800000u;
+  if (FMT == 1) return (b & 0x7FFFu) > 0x7F80u;
+  return (b & 0x7FFFu) > 0x7C00u;
 }
-template <> __device__ __forceinline__ uint32_t load_key<uint32_t>(const uint32_t* p) {
-  return key32(*p);
+template <int FMT, typename T>
+__device__ __forceinline__ uint32_t load_key(const T* p) {
+  const uint32_t b = static_cast<uint32_t>(*p);
+  if (is_nan_bits<FMT>(b)) return 0u;
+  return FMT == 0 ? key32(b) : (keys16(b) & 0xFFFFu);
 }
 
-template <typename T>
+template <typename T, int FMT>
 __global__ void __launch_bounds__(4 * 32)
 wta_fwd_generic_kernel(const T* __restrict__ x, int64_t n_rows, int d, int64_t row_stride,
                        int k_host, const int32_t* __restrict__ k_dev, int exact,
@@ -348,12 +409,15 @@ wta_fwd_generic_kernel(const T* __restrict__ x, int64_t n_rows, int d, int64_t r
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + warp; row < n_rows;
        row += static_cast<int64_t>(gridDim.x) * 4) {
     const T* xr = x + row * row_stride;
+    int nan_count = 0;
+    for (int j = lane; j < d; j += 32) nan_count += is_nan_bits<FMT>(static_cast<uint32_t>(xr[j]));
+    int kk = k - static_cast<int>(__reduce_add_sync(kFull, static_cast<uint32_t>(nan_count)));
+    const bool none = kk <= 0;
     uint32_t prefix = 0;
-    int kk = k;
-    for (int p = 0; p < KB / 8; ++p) {
+    for (int p = 0; p < KB / 8 && !none; ++p) {
       const int shift = KB - 8 * (p + 1);
       for (int j = lane; j < d; j += 32) {
-        const uint32_t key = load_key(xr + j);
+        const uint32_t key = load_key<FMT>(xr + j);
         const bool match = (p == 0) || ((key >> (shift + 8)) == prefix);
         const uint32_t bin = match ? ((key >> shift) & 0xFFu) : 256u;
         hist[bin * 32 + lane] += 1;
@@ -365,15 +429,16 @@ wta_fwd_generic_kernel(const T* __restrict__ x, int64_t n_rows, int d, int64_t r
       prefix = (prefix << 8) | static_cast<uint32_t>(b);
       kk -= above;
     }
-    const uint32_t t = prefix;
+    // with no winners the threshold is above every key
+    const uint32_t t = none ? (KB == 16 ? 0x10000u : 0xFFFFFFFFu) : prefix;
     uint32_t tlo = t, thi = t;
     const uint32_t pz = (KB == 16) ? 0x8000u : 0x80000000u, nz = pz - 1u;
     if (t == pz || t == nz) { tlo = nz; thi = pz; }
     int need = 0;
     if (exact) {
       int gt = 0;
-      for (int j = lane; j < d; j += 32) gt += load_key(xr + j) > thi;
-      need = k - static_cast<int>(__reduce_add_sync(kFull, static_cast<uint32_t>(gt)));
+      for (int j = lane; j < d; j += 32) gt += load_key<FMT>(xr + j) > thi;
+      need = none ? 0 : k - static_cast<int>(__reduce_add_sync(kFull, static_cast<uint32_t>(gt)));
     }
     int rank = 0;
     uint8_t* mrow = bitmask + row * mbytes;
@@ -381,7 +446,7 @@ wta_fwd_generic_kernel(const T* __restrict__ x, int64_t n_rows, int d, int64_t r
       const int j = j0 + lane;
       bool keep = false;
       if (j < d) {
-        const uint32_t key = load_key(xr + j);
+        const uint32_t key = load_key<FMT>(xr + j);
         keep = exact ? (key > thi) : (key >= tlo);
         const bool tie = exact && key >= tlo && key <= thi;
         const uint32_t tb = __ballot_sync(__activemask(), tie);
@@ -450,12 +515,12 @@ __global__ void k_from_logits_kernel(const float* __restrict__ logits, int64_t n
   k_out[i] = static_cast<int32_t>(k);
 }
 
-template <int CH, bool EXACT, bool WRITE_Y, bool HIST>
+template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST>
 int launch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, const int32_t* k_dev,
                  void* y, uint8_t* bitmask, int32_t* win, cudaStream_t st) {
-  auto kern = wta_fwd16_kernel<CH, EXACT, WRITE_Y, HIST>;
-  const size_t smem = kFastWarps * kPairHistBytes + (HIST ? 256 * CH * 4 : 0);
-  TDX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  auto kern = wta_fwd16_kernel<CH, BF, EXACT, WRITE_Y, HIST>;
+  const size_t smem = HIST ? 256 * CH * 4 : 0;
+  if (smem) TDX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
   TDX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFastWarps * 32, smem));
   per_sm = per_sm < 1 ? 1 : per_sm;
@@ -468,19 +533,34 @@ int launch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, const
   return check_launch("wta_fwd16_kernel");
 }
 
-template <int CH>
+template <int CH, bool BF>
 int dispatch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, const int32_t* k_dev,
                    int mode, void* y, uint8_t* bitmask, int32_t* win, cudaStream_t st) {
   const bool exact = mode == TAU_DXB_WTA_EXACT_K, wy = y != nullptr, h = win != nullptr;
 #define TDX_WTA_CASE(E, W, H)                                                        \
   if (exact == E && wy == W && h == H)                                               \
-    return launch_fwd16<CH, E, W, H>(x, n_rows, row_stride, k, k_dev, y, bitmask, win, st);
+    return launch_fwd16<CH, BF, E, W, H>(x, n_rows, row_stride, k, k_dev, y, bitmask, win, st);
   TDX_WTA_CASE(false, true, false) TDX_WTA_CASE(false, false, false)
   TDX_WTA_CASE(false, true, true)  TDX_WTA_CASE(false, false, true)
   TDX_WTA_CASE(true, true, false)  TDX_WTA_CASE(true, false, false)
   TDX_WTA_CASE(true, true, true)   TDX_WTA_CASE(true, false, true)
 #undef TDX_WTA_CASE
   return fail(TAU_DXB_ERR_UNSUPPORTED, "wta_fwd: no kernel for this mode");
+}
+
+template <bool BF>
+int dispatch_fwd16_width(int64_t d, const void* x, int64_t n_rows, int64_t row_stride, int k,
+                         const int32_t* k_dev, int mode, void* y, uint8_t* bitmask, int32_t* win,
+                         cudaStream_t st) {
+  switch (d / 256) {
+    case 3:  return dispatch_fwd16<3, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
+    case 4:  return dispatch_fwd16<4, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
+    case 6:  return dispatch_fwd16<6, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
+    case 8:  return dispatch_fwd16<8, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
+    case 12: return dispatch_fwd16<12, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
+    case 16: return dispatch_fwd16<16, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
+    default: return 1;   // no fast kernel for this width
+  }
 }
 
 }  // namespace
@@ -498,15 +578,10 @@ int wta_fwd_impl(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (row_stride % 8 == 0) &&
                        (!y || reinterpret_cast<uintptr_t>(y) % 16 == 0);
   if (dtype != TAU_DXB_F32 && aligned && d % 256 == 0) {
-    switch (d / 256) {
-      case 3:  return dispatch_fwd16<3>(x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st);
-      case 4:  return dispatch_fwd16<4>(x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st);
-      case 6:  return dispatch_fwd16<6>(x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st);
-      case 8:  return dispatch_fwd16<8>(x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st);
-      case 12: return dispatch_fwd16<12>(x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st);
-      case 16: return dispatch_fwd16<16>(x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st);
-      default: break;
-    }
+    const int rc = dtype == TAU_DXB_BF16
+        ? dispatch_fwd16_width<true>(d, x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st)
+        : dispatch_fwd16_width<false>(d, x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st);
+    if (rc <= 0) return rc;        // launched (or failed); 1 = width without a fast kernel
   }
   const size_t smem = 4 * kHist16Bytes;
   int64_t blocks = (n_rows + 3) / 4;
@@ -514,13 +589,13 @@ int wta_fwd_impl(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_
   if (blocks > cap) blocks = cap;
   const int exact = mode == TAU_DXB_WTA_EXACT_K;
   if (dtype == TAU_DXB_F32) {
-    auto kern = wta_fwd_generic_kernel<uint32_t>;
+    auto kern = wta_fwd_generic_kernel<uint32_t, 0>;
     TDX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     kern<<<static_cast<unsigned>(blocks), 128, smem, st>>>(
         static_cast<const uint32_t*>(x), n_rows, static_cast<int>(d), row_stride, kk, k_dev, exact,
         static_cast<uint32_t*>(y), bitmask, win);
   } else {
-    auto kern = wta_fwd_generic_kernel<uint16_t>;
+    auto kern = dtype == TAU_DXB_BF16 ? wta_fwd_generic_kernel<uint16_t, 1> : wta_fwd_generic_kernel<uint16_t, 2>;
     TDX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     kern<<<static_cast<unsigned>(blocks), 128, smem, st>>>(
         static_cast<const uint16_t*>(x), n_rows, static_cast<int>(d), row_stride, kk, k_dev, exact,

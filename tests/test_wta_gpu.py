@@ -197,3 +197,46 @@ def test_autograd_ste_and_exact_function(W):
 def test_cpu_tensor_raises(W):
     with pytest.raises(RuntimeError):
         W.wta_fused_forward(torch.randn(2, 3072), 10)
+
+
+@pytest.mark.parametrize("d,dtype", [(3072, torch.bfloat16), (3072, torch.float16), (1000, torch.bfloat16),
+                                     (3072, torch.float32)])
+def test_nan_rows_follow_reference_semantics(W, d, dtype):
+    """NaN sorts largest in the reference's topk / kthvalue and then fails
+    x >= thr: the threshold is the (k - #NaN)-th largest non-NaN value, NaN is
+    never kept, and a row with #NaN >= k keeps nothing. The fast and generic
+    paths agree with the oracle on such rows."""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn(64, d, device=DEV, generator=g).to(dtype)
+    x[0, ::7] = float("nan")
+    x[1] = float("nan")
+    x[1, :5] = 1.0
+    x[2, :20] = float("nan")
+    x[2, 20:] = -float("inf")
+    x[3, 100] = float("nan")
+    x[3, 200] = float("inf")
+    x[4] = torch.randn(d, device=DEV, generator=g).to(dtype) * 1e-39 if dtype != torch.float16 else x[4]
+    xf = x.float().cpu().numpy()
+    for k in (1, 5, 19, 21, 306, d):
+        kk = min(k, d)
+        for mode, ref_fn in ((W.THRESHOLD, OW.threshold_mask), (W.EXACT_K, OW.exact_k_mask)):
+            y, bits = W.wta_select(x, kk, mode)
+            mine = W.unpack_mask(bits, d).cpu().numpy()
+            assert np.array_equal(mine, ref_fn(xf, kk)), (d, dtype, k, mode)
+
+
+def test_threshold_search_rows_of_mixed_scale(W):
+    """Consecutive rows with very different thresholds (the fast path starts
+    each search at the previous row's threshold of its warp)."""
+    g = torch.Generator(device=DEV).manual_seed(6)
+    base = torch.randn(4096, 3072, device=DEV, generator=g)
+    scale = torch.logspace(-20, 20, 4096, device=DEV)[torch.randperm(4096, device=DEV, generator=g)]
+    x = (base * scale[:, None]).to(torch.bfloat16)
+    x[::3] = x[::3].abs()
+    x[1::5] = -x[1::5].abs()
+    for k in (1, 306, 1536, 3072):
+        y, bits = W.wta_select(x, k, W.THRESHOLD)
+        thr = x.float().kthvalue(3072 - k + 1, dim=-1, keepdim=True).values
+        keep = x.float() >= thr
+        assert torch.equal(W.unpack_mask(bits, 3072), keep), k
+        assert torch.equal(y, torch.where(keep, x, torch.zeros_like(x))), k
