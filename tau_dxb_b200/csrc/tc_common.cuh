@@ -315,6 +315,19 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return r;
 }
 
+// three-input max (NaN operands are ignored, as by fmaxf)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// 0xFFFFFFFF if a == b (ordered), else 0
+__device__ __forceinline__ uint32_t eq_mask(float a, float b) {
+  uint32_t d;
+  asm("set.eq.u32.f32 %0, %1, %2;" : "=r"(d) : "f"(a), "f"(b));
+  return d;
+}
+
 // ---- packed fp32 pairs (fma/mul/add .f32x2: two lanes per issued instruction)
 __device__ __forceinline__ uint64_t f2_bits(float2 a) {
   uint64_t r;
