@@ -1,7 +1,9 @@
 // tau-opus attention backward, tensor-core path for sm_100a (bf16, D = 64).
 //
 // One CTA owns a 128-key tile of one (b, h) and streams every 128-row query
-// tile through it (K, V loaded once; Q_i, dO_i double-buffered by TMA):
+// tile through it (K, V loaded once; Q_i, dO_i and the row statistics in a
+// three-stage TMA ring, so the loads for tile i+2 are in flight while tile i
+// is processed):
 //   S^T  = K Q_i^T          (M=128 keys, N=128 queries, K=64)   -> TMEM [0,128)
 //   dP^T = V dO_i^T         (M=128,      N=128,         K=64)   -> TMEM [128,256)
 //   elementwise, one thread per key row: P = q / Z and
@@ -14,7 +16,8 @@
 //   dV  += P^T dO_i         (M=128 keys, N=64, K=128 queries; A from TMEM) -> [256,320)
 //   dK  += dS^T Q_i         (A = dS^T K-major in shared memory)            -> [320,384)
 //   dQ_i = dS K             (M=128 queries; the same dS^T tile as MN-major A) -> [384,448)
-//   dQ_i leaves through a TMA bulk reduce-add into the fp32 dQ accumulator.
+//   dQ_i leaves through TMA bulk reduce-adds into the fp32 dQ accumulator,
+//   32 columns at a time through one 16 KB staging box.
 // Warp roles (24 warps): 0 TMA, 1 MMA + TMEM owner, 2 row statistics of each
 // query tile, 4-7 dQ epilogue (and the final dK / dV store), 8-23 elementwise
 // (four groups of 4 warps, 32 query columns each).
@@ -66,6 +69,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kLog2Clamp = -26.575424759098897f;   // log2(1e-8)
 constexpr int kErrTimeoutTma = 1, kErrTimeoutMma = 2, kErrTimeoutCompute = 4;
+constexpr int kQStages = 3;                   // Q / dO / row-statistics ring
 
 struct BwdParams {
   CUtensorMap tq, tk, tv, tdo, tdq;
@@ -84,8 +88,8 @@ struct BwdParams {
 
 struct __align__(8) BwdBarriers {
   uint64_t kv_full;
-  uint64_t qd_full[2];
-  uint64_t qd_empty[2];
+  uint64_t qd_full[kQStages];
+  uint64_t qd_empty[kQStages];
   uint64_t s_full;
   uint64_t s_free;
   uint64_t ds_ready;
@@ -103,12 +107,12 @@ struct __align__(8) BwdBarriers {
 
 constexpr uint32_t kOffK = 0;
 constexpr uint32_t kOffV = kOffK + kTile;
-constexpr uint32_t kOffQ = kOffV + kTile;           // 2 stages
-constexpr uint32_t kOffDO = kOffQ + 2 * kTile;      // 2 stages
-constexpr uint32_t kOffDS = kOffDO + 2 * kTile;     // dS^T, 2 buffers x 2 atoms of 64 queries
-constexpr uint32_t kOffStage = kOffDS + 4 * kTile;  // dQ staging, 2 boxes [128][32] fp32
-constexpr uint32_t kOffStats = kOffStage + 2 * kTile;   // 2 stages x {mc, rz, dq} x 128 fp32
-constexpr uint32_t kOffBar = kOffStats + 2 * 3 * kT * 4;
+constexpr uint32_t kOffQ = kOffV + kTile;                 // kQStages stages
+constexpr uint32_t kOffDO = kOffQ + kQStages * kTile;     // kQStages stages
+constexpr uint32_t kOffDS = kOffDO + kQStages * kTile;    // dS^T, 2 buffers x 2 atoms of 64 queries
+constexpr uint32_t kOffStage = kOffDS + 4 * kTile;        // dQ staging, one box [128][32] fp32
+constexpr uint32_t kOffStats = kOffStage + kTile;         // kQStages x {mc, rz, dq} x 128 fp32
+constexpr uint32_t kOffBar = kOffStats + kQStages * 3 * kT * 4;
 constexpr uint32_t kBwdSmem = kOffBar + sizeof(BwdBarriers) + 1024;
 
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 320, kColDQ = 384, kColP = 448;
@@ -151,9 +155,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
 
   if (threadIdx.x == 0) {
     tc::mbar_init(&bars->kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      tc::mbar_init(&bars->qd_full[s], 2);
+    for (int s = 0; s < kQStages; ++s) {
+      tc::mbar_init(&bars->qd_full[s], 2);               // TMA bytes + row-statistics warp
       tc::mbar_init(&bars->qd_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       tc::mbar_init(&bars->ds_free[s], 1 + 4);          // MMA commit + 4 epilogue warps
       tc::mbar_init(&bars->ds_full_epi[s], kComputeWarps);
     }
@@ -190,20 +196,20 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       tc::tma_load_4d(smem + kOffK, &p.tk, &bars->kv_full, 0, k0, h, b);
       tc::tma_load_4d(smem + kOffV, &p.tv, &bars->kv_full, 0, k0, h, b);
       int issued = 0;
-      for (int i = 0; i < nQ; ++i) {
-        const int s = i & 1;
-        if (i >= 2 && !tc::mbar_wait(&bars->qd_empty[s], ((i >> 1) - 1) & 1, abort_flag, p.err, kErrTimeoutTma))
+      for (int i = 0, s = 0, ph = 0; i < nQ; ++i) {    // stage s of tile i, ph = (i / kQStages) & 1
+        if (i >= kQStages && !tc::mbar_wait(&bars->qd_empty[s], ph ^ 1, abort_flag, p.err, kErrTimeoutTma))
           break;
         tc::mbar_arrive_expect_tx(&bars->qd_full[s], 2 * kTile);
         tc::tma_load_4d(smem + kOffQ + s * kTile, &p.tq, &bars->qd_full[s], 0, i * kT, h, b);
         tc::tma_load_4d(smem + kOffDO + s * kTile, &p.tdo, &bars->qd_full[s], 0, i * kT, h, b);
         issued = i + 1;
+        if (++s == kQStages) { s = 0; ph ^= 1; }
       }
       if (*abort_flag) {   // let started copies land before the CTA exits
         const uint64_t t0 = tc::globaltimer_ns();
-        for (int i = (issued > 2 ? issued - 2 : 0); i < issued; ++i) {
-          const uint32_t a = tc::smem_u32(&bars->qd_full[i & 1]);
-          while (!tc::mbar_try_wait(a, (i >> 1) & 1) && tc::globaltimer_ns() - t0 < tc::kWaitLimitNs) {
+        for (int i = (issued > kQStages ? issued - kQStages : 0); i < issued; ++i) {
+          const uint32_t a = tc::smem_u32(&bars->qd_full[i % kQStages]);
+          while (!tc::mbar_try_wait(a, (i / kQStages) & 1) && tc::globaltimer_ns() - t0 < tc::kWaitLimitNs) {
           }
         }
         const uint32_t a = tc::smem_u32(&bars->kv_full);
@@ -226,10 +232,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       const uint32_t kK = tc::sdesc_lo(sK, 16), kV = tc::sdesc_lo(sV, 16), mK = tc::sdesc_lo(sK, 16384);
       constexpr uint32_t tileStep = kTile >> 4;
       bool ok = tc::mbar_wait(&bars->kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
+      int s = 0, ph = 0, qj = 0;       // ring stage / phase of tile i; stage of tile i - 1
       for (int i = 0; i <= nQ && ok; ++i) {
         if (i < nQ) {
-          const int s = i & 1;
-          ok = tc::mbar_wait(&bars->qd_full[s], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma);
+          ok = tc::mbar_wait(&bars->qd_full[s], ph, abort_flag, p.err, kErrTimeoutMma);
           if (ok && i > 0) ok = tc::mbar_wait(&bars->s_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
           if (!ok) break;
           tc::tc_fence_after();
@@ -248,8 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           if (ok && j > 0) ok = tc::mbar_wait(&bars->dq_free, (j - 1) & 1, abort_flag, p.err, kErrTimeoutMma);
           if (!ok) break;
           tc::tc_fence_after();
-          const uint32_t mDO = tc::sdesc_lo(sDO, 16384) + sj * tileStep;
-          const uint32_t mQ = tc::sdesc_lo(sQ, 16384) + sj * tileStep;
+          const uint32_t mDO = tc::sdesc_lo(sDO, 16384) + qj * tileStep;
+          const uint32_t mQ = tc::sdesc_lo(sQ, 16384) + qj * tileStep;
           const uint32_t kDS = tc::sdesc_lo(sDS, 16) + sj * 2 * tileStep;
           const uint32_t mDS = tc::sdesc_lo(sDS, 16384) + sj * 2 * tileStep;
           const bool acc0 = j > 0;
@@ -265,9 +271,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           for (int kk = 0; kk < kT / 16; ++kk)      // dQ_j = dS K
             tc::umma_f16_ss2(tmem + kColDQ, mDS + 128 * kk, hi, mK + 128 * kk, hi, idQ, kk > 0);
           tc::umma_commit(&bars->ds_free[sj]);
-          tc::umma_commit(&bars->qd_empty[sj]);
+          tc::umma_commit(&bars->qd_empty[qj]);
           tc::umma_commit(&bars->dq_full);
         }
+        qj = s;
+        if (++s == kQStages) { s = 0; ph ^= 1; }
       }
       tc::umma_commit(&bars->fin);
       tc::umma_commit(&bars->drain);
@@ -279,10 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
   } else if (warp == 2) {
     // ---------------------------------------------------------------- row statistics
     const float al2 = alpha * kLog2e;
-    for (int i = 0; i < nQ; ++i) {
-      const int s = i & 1;
-      if (i >= 2 && !__all_sync(0xffffffffu, tc::mbar_wait(&bars->qd_empty[s], ((i >> 1) - 1) & 1,
-                                                            abort_flag, p.err, kErrTimeoutTma)))
+    for (int i = 0, s = 0, ph = 0; i < nQ; ++i, s = (s + 1 == kQStages ? 0 : s + 1), ph ^= (s == 0)) {
+      if (i >= kQStages && !__all_sync(0xffffffffu, tc::mbar_wait(&bars->qd_empty[s], ph ^ 1,
+                                                                   abort_flag, p.err, kErrTimeoutTma)))
         break;
       float* st = stats + s * 3 * kT;
       // all 12 loads of this lane in flight at once (one round of global latency)
@@ -310,16 +317,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
   } else if (warp < 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 48;" ::: "memory");
     // ---------------------------------------------------------------- dQ epilogue
-    // One thread per query row; 32 TMEM columns in registers at a time.
+    // One thread per query row; dQ_j's 64 TMEM columns in two halves of 32,
+    // each scaled by tau*alpha, staged in one 128B-swizzled box and sent with
+    // a TMA bulk reduce-add (thread 128 issues it and waits for the box to be
+    // read before it is refilled).
     const int r = ((warp & 3) << 5) + lane;
     const float ta = tau * alpha;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) << 5) << 16;
     uint8_t* stage = smem + kOffStage;
     bool ok = true;
     for (int j = 0; j < nQ && ok; ++j) {
-      // the previous reduce must have finished reading the staging buffer
-      if (threadIdx.x == 128) tc::bulk_wait_group_read0();
-      // one decision for the whole group (it meets again at a named barrier below)
+      // one decision for the whole group (it meets again at named barriers below)
       ok = tc::named_barrier_and(1, 128, tc::mbar_wait(&bars->dq_full, j & 1, abort_flag, p.err,
                                                        kErrTimeoutCompute));
       if (!ok) break;
@@ -329,23 +337,27 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         uint32_t a[32];
         tc::tmem_ld32(tmem + lane_base + kColDQ + 32 * half, a);
         tc::tmem_wait_ld_regs(a);
+        if (half == 1) {         // every TMEM read of dQ_j is done
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bars->dq_free);
+        }
+        // the previous reduce must have finished reading the box
+        if (threadIdx.x == 128) tc::bulk_wait_group_read0();
+        tc::named_barrier_sync(1, 128);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int pc = (u ^ (r & 7)) << 4;
-          *reinterpret_cast<float4*>(stage + half * kTile + r * 128 + pc) =
+          *reinterpret_cast<float4*>(stage + r * 128 + pc) =
               make_float4(__uint_as_float(a[4 * u]) * ta, __uint_as_float(a[4 * u + 1]) * ta,
                           __uint_as_float(a[4 * u + 2]) * ta, __uint_as_float(a[4 * u + 3]) * ta);
         }
-      }
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars->dq_free);
-      tc::fence_async_smem();
-      tc::named_barrier_sync(1, 128);
-      if (threadIdx.x == 128) {
-        tc::tma_reduce_add_3d(&p.tdq, stage, 0, j * kT, static_cast<int>(bh));
-        tc::tma_reduce_add_3d(&p.tdq, stage + kTile, 32, j * kT, static_cast<int>(bh));
-        tc::bulk_commit_group();
+        tc::fence_async_smem();
+        tc::named_barrier_sync(1, 128);
+        if (threadIdx.x == 128) {
+          tc::tma_reduce_add_3d(&p.tdq, stage, 32 * half, j * kT, static_cast<int>(bh));
+          tc::bulk_commit_group();
+        }
       }
       // rowsum_keys(F) of query r from the bf16 dS^T tile (key rows, 128B-swizzled)
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->ds_full_epi[j & 1], (j >> 1) & 1, abort_flag,
@@ -382,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       const int q = j * kT + (r >> 6) * 64 + c8 * 8 + kp;
       if (q < p.Lq) atomicAdd(p.ws_rowf + bh * p.Lq + q, v[0] * ta);
     }
+    if (threadIdx.x == 128) tc::bulk_wait_group0();
     // final dK / dV (one thread per key row)
     if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&bars->fin, 0, abort_flag, p.err, kErrTimeoutCompute));
     if (ok) {
@@ -416,7 +429,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         }
       }
     }
-    if (threadIdx.x == 128) tc::bulk_wait_group0();
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 96;" ::: "memory");
     // ---------------------------------------------------------------- elementwise
@@ -456,10 +468,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     const bool tile_full = k0 + kT <= p.Lk;
     const bool has_mask = p.mask != nullptr || p.causal;
     float2 acc_tau = make_float2(0.f, 0.f), acc_alpha = make_float2(0.f, 0.f);
+    int qs = 0, qph = 0;             // stage and phase of tile i in the Q / dO / statistics ring
     auto chunk_math = [&](auto masked_c, auto full_c, const uint32_t (&rr)[32], int i, int col0,
                           uint32_t (&pp)[8], uint32_t (&pf)[8]) {
       constexpr bool kMasked = decltype(masked_c)::value, kFull = decltype(full_c)::value;
-      const float* stc = stats + (i & 1) * 3 * kT;
+      const float* stc = stats + qs * 3 * kT;
       float mv[kMasked ? 16 : 1];
       if constexpr (kMasked) {
 #pragma unroll
@@ -513,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     bool ok = true;
     for (int i = 0; i < nQ && ok; ++i) {
       const int s = i & 1;
-      ok = tc::mbar_wait(&bars->qd_full[s], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutCompute);
+      ok = tc::mbar_wait(&bars->qd_full[qs], qph, abort_flag, p.err, kErrTimeoutCompute);
       ok = ok && tc::mbar_wait(&bars->s_full, i & 1, abort_flag, p.err, kErrTimeoutCompute);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -570,6 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         tc::mbar_arrive(&bars->ds_ready);
         tc::mbar_arrive(&bars->ds_full_epi[s]);
       }
+      if (++qs == kQStages) { qs = 0; qph ^= 1; }
     }
     float sum_tau = acc_tau.x + acc_tau.y, sum_alpha = acc_alpha.x + acc_alpha.y;
 #pragma unroll

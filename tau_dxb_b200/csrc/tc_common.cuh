@@ -315,6 +315,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return r;
 }
 
+// fire-and-forget fp32 vector add into global memory (16-byte aligned)
+__device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" :: "l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 // three-input max (NaN operands are ignored, as by fmaxf)
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
@@ -329,35 +335,12 @@ __device__ __forceinline__ uint32_t eq_mask(float a, float b) {
 }
 
 // ---- packed fp32 pairs (fma/mul/add .f32x2: two lanes per issued instruction)
-__device__ __forceinline__ uint64_t f2_bits(float2 a) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
-  return r;
-}
-__device__ __forceinline__ float2 bits_f2(uint64_t r) {
-  float2 a;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(r));
-  return a;
-}
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
-  return bits_f2(d);
-}
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-  return bits_f2(d);
-}
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-  return bits_f2(d);
-}
+// The compiler builtins, so that register pairs are allocated without moves.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-  return bits_f2(d);
+  return __fadd2_rn(a, make_float2(-b.x, -b.y));
 }
 
 template <int N>
@@ -374,9 +357,5 @@ __device__ __forceinline__ float horner(const float (&c)[N], float x) {
 // 128-byte swizzle. Returns false (with a message) if the driver rejects it.
 bool make_tmap_bhld(CUtensorMap* map, const void* base, int64_t D, int64_t L, int64_t H, int64_t B,
                     const int64_t strides_elems[4], int box_rows);
-
-// host: 3-D fp32 tensor map over a contiguous [planes][rows][64] array with a
-// box of 32 x box_rows x 1 and 128-byte swizzle (the dQ accumulator).
-bool make_tmap_f32_rows64(CUtensorMap* map, void* base, int64_t rows, int64_t planes, int box_rows);
 
 }  // namespace taudxb
