@@ -115,6 +115,40 @@ def synthetic_batch(cfg: StepConfig, device, generator: torch.Generator):
     return mel.to(device, non_blocking=True), labels.to(device, non_blocking=True)
 
 
+class PaddedHeadLoss(torch.nn.Module):
+    """Whisper forward + the reference's loss (echo/train_echo_opus1.py:405-420:
+    cross-entropy of the LM head over the vocabulary, labels -100 ignored), with
+    the tied LM head evaluated over a vocabulary padded to a multiple of 64.
+
+    The 51865-wide logits of the plain head have an odd row pitch, which keeps
+    the three head GEMMs (logits, their input and weight gradients; ~0.57 TFLOP
+    each at batch 16) off the aligned tensor-core kernels. Here the head weight
+    gets zero rows and a bias of -inf on the pad columns: the pad logits drop
+    out of the softmax exactly, so the loss and every gradient equal the
+    unpadded head's."""
+
+    def __init__(self, model, multiple: int = 64):
+        super().__init__()
+        self.whisper = model
+        v = model.config.vocab_size
+        self.vocab = v
+        self.pad = (-v) % multiple
+        bias = torch.zeros(v + self.pad)
+        bias[v:] = float("-inf")
+        self.register_buffer("head_bias", bias, persistent=False)
+
+    def forward(self, input_features, labels):
+        from transformers.models.whisper.modeling_whisper import shift_tokens_right
+        cfg = self.whisper.config
+        dec_in = shift_tokens_right(labels, cfg.pad_token_id, cfg.decoder_start_token_id)
+        h = self.whisper.model(input_features, decoder_input_ids=dec_in).last_hidden_state
+        w = self.whisper.proj_out.weight
+        if self.pad:
+            w = torch.nn.functional.pad(w, (0, 0, 0, self.pad))
+        logits = torch.nn.functional.linear(h, w, self.head_bias.to(w.dtype))
+        return torch.nn.functional.cross_entropy(logits.view(-1, logits.shape[-1]), labels.reshape(-1))
+
+
 class TrainStep:
     """One fine-tune step on this rank (DDP-wrapped when a process group exists)."""
 
@@ -123,10 +157,10 @@ class TrainStep:
         self.device = torch.device(device)
         self.model = build_model(cfg, self.device, tau_init)
         self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
-        self.net = self.model
+        self.net = PaddedHeadLoss(self.model).to(self.device)
         if self.world > 1:
             from torch.nn.parallel import DistributedDataParallel as DDP
-            self.net = DDP(self.model, device_ids=[self.device.index] if self.device.type == "cuda" else None,
+            self.net = DDP(self.net, device_ids=[self.device.index] if self.device.type == "cuda" else None,
                            bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True,
                            broadcast_buffers=False)
         self.opt = make_optimizer(self.model, cfg)
@@ -135,7 +169,7 @@ class TrainStep:
     def loss(self, mel, labels):
         amp = torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.device.type == "cuda")
         with amp:
-            ce = self.net(input_features=mel, labels=labels).loss
+            ce = self.net(mel, labels)
             sp = SG.get_sparsity_loss().to(ce.device)
             return ce + self.cfg.sparsity_lambda * sp, ce
 

@@ -52,8 +52,8 @@ def _worker(rank, world, port, tests_dir, mode):
             ref = {}
             for b in batches:
                 step.model.zero_grad(set_to_none=True)
-                l, _ = T.TrainStep.loss(type("S", (), {"net": step.model, "device": step.device,
-                                                       "cfg": cfg})(), *b)
+                l, _ = T.TrainStep.loss(type("S", (), {"net": T.PaddedHeadLoss(step.model),
+                                                       "device": step.device, "cfg": cfg})(), *b)
                 l.backward()
                 for n, p in step.model.named_parameters():
                     if p.grad is not None:

@@ -153,3 +153,28 @@ def test_prune_low_winners_masks_gradients(patched):
 def test_step_flops_formula():
     from tau_dxb_b200.train import StepConfig, model_flops_per_step
     assert model_flops_per_step(StepConfig()) / 1e12 == pytest.approx(26.79, abs=0.01)
+
+
+def test_padded_head_loss_equals_the_plain_head():
+    """The train step's LM head over a vocabulary padded to a multiple of 64
+    (zero weight rows, -inf bias) gives HF Whisper's own loss and gradients."""
+    from tau_dxb_b200 import train as T
+    cfg = T.StepConfig(batch=2, frames=200, label_len=16, min_label=6, encoder_layers=1,
+                       decoder_layers=1, d_model=64, heads=2, ffn=128, vocab=300)
+    torch.manual_seed(0)
+    from transformers import WhisperForConditionalGeneration
+    model = WhisperForConditionalGeneration(T.whisper_config(cfg)).double()
+    mel, labels = T.synthetic_batch(cfg, "cpu", torch.Generator().manual_seed(3))
+    mel = mel.double()
+    ref = model(input_features=mel, labels=labels).loss
+    ref.backward()
+    g_ref = {n: p.grad.clone() for n, p in model.named_parameters() if p.grad is not None}
+    model.zero_grad(set_to_none=True)
+    head = T.PaddedHeadLoss(model)
+    assert head.pad == 20
+    loss = head(mel, labels)
+    loss.backward()
+    assert torch.allclose(loss, ref, rtol=1e-12, atol=1e-12)
+    for n, p in model.named_parameters():
+        if n in g_ref:
+            assert torch.allclose(p.grad, g_ref[n], rtol=1e-10, atol=1e-12), n
