@@ -315,8 +315,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
     bool ok = true;
     int i = 0;
     // pass 1 maxima: mraw over fast chunks (raw QK^T, scale > 0 keeps the
-    // order), mlim over the others (scaled, masked scores)
+    // order), mlim over the others (scaled, masked scores); mchunk is the
+    // first fast 16-key chunk (4 key tile + chunk) that reached mraw
     float mraw = -INFINITY, mlim = -INFINITY;
+    int mchunk = -1;
     // Per key tile the warp takes one of three branch-free element paths:
     // kFast (every key of its half valid and unmasked for all 32 rows, no mask
     // tensor, scale > 0), kLimited (causal limit / padding per row, no mask
@@ -330,7 +332,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
     // Pass 1: exact row max of s = scale * QK^T (+ mask), three-input max
     // trees. The first argmax is found in pass 2, which recomputes S with the
     // same MMA on the same tiles (bit-identical scores): the first key whose
-    // score equals the max.
+    // score equals the max. For fast chunks only the chunk pass 1 recorded is
+    // searched.
     auto score_x = [&](auto mode_c, float raw, int key) -> float {
       constexpr int kMode = decltype(mode_c)::value;
       if constexpr (kMode == kFast) {
@@ -345,7 +348,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
         return key < p.Lk ? sv : -INFINITY;
       }
     };
-    auto pass1_chunk = [&](auto mode_c, const uint32_t (&v)[16], int key0) {
+    auto pass1_chunk = [&](auto mode_c, const uint32_t (&v)[16], int key0, int cid) {
       constexpr int kMode = decltype(mode_c)::value;
       float x[16];
 #pragma unroll
@@ -354,8 +357,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
       const float c2 = tc::max3(x[6], x[7], x[8]), c3 = tc::max3(x[9], x[10], x[11]);
       const float c4 = tc::max3(x[12], x[13], x[14]);
       const float cx = tc::max3(tc::max3(c0, c1, c2), c3, c4);
-      if constexpr (kMode == kFast) mraw = tc::max3(mraw, cx, x[15]);
-      else mlim = tc::max3(mlim, cx, x[15]);
+      if constexpr (kMode == kFast) {
+        const float cm = fmaxf(cx, x[15]);
+        if (cm > mraw) {                 // strictly larger: the first chunk holding the max
+          mraw = cm;
+          mchunk = cid;
+        }
+      } else {
+        mlim = tc::max3(mlim, cx, x[15]);
+      }
     };
     auto release_s = [&]() {      // every TMEM read of S for this step is done
       tc::tc_fence_before();
@@ -385,7 +395,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
       tc::tc_fence_after();
       const int mode = tile_mode(j);
       auto run = [&](auto mode_c) {
-        sweep([&](const uint32_t (&v)[16], int c) { pass1_chunk(mode_c, v, j * kBN + kh + 16 * c); });
+        sweep([&](const uint32_t (&v)[16], int c) { pass1_chunk(mode_c, v, j * kBN + kh + 16 * c, 4 * j + c); });
       };
       if (mode == kFast) run(IntC<kFast>{});
       else if (mode == kLimited) run(IntC<kLimited>{});
@@ -421,7 +431,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
       return tc::ex2(fmaxf(y, ylo));
     };
     int j2 = 0;                    // key tile of the current pass-2 step
-    auto pass2_chunk = [&](auto mode_c, const uint32_t (&v)[16], int c, int key0) {
+    auto pass2_chunk = [&](auto mode_c, const uint32_t (&v)[16], int c, int key0, int cid) {
       constexpr int kMode = decltype(mode_c)::value;
       uint32_t pk[8];
       uint32_t eq = 0;             // keys of this chunk whose score equals the max
@@ -434,7 +444,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
           const int key = key0 + e + u;
           if constexpr (kMode == kFast) {
             qq[u] = qval(fmaf(raw, sa2, -ma2));
-            eq |= tc::eq_mask(raw, traw) & (1u << (e + u));
           } else if constexpr (kMode == kLimited) {
             // masked: ((s + finfo.min) - m) alpha log2(e), rounded as the reference
             const float a2 = key < lim_c ? fmaf(raw, sa2, -ma2) : (raw * p.scale + kMaskMin - m) * al2;
@@ -453,6 +462,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
         l0 += qq[0];
         l1 += qq[1];
         pk[e >> 1] = tc::pack_bf16(qq[0], qq[1]);
+      }
+      if constexpr (kMode == kFast) {
+        if (cid == mchunk) {             // the chunk that holds this half's first fast max
+          // bit e of the sum = (raw_e == traw); 1.0 / 0.0 flags, FMA-pipe accumulation
+          float acc = 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) acc = fmaf(tc::eq_flag(__uint_as_float(v[e]), traw), float(1 << e), acc);
+          eq = __float_as_uint(acc + 8388608.f) & 0xFFFFu;
+        }
       }
       if (eq != 0 && amax == INT_MAX) amax = key0 + __ffs(eq) - 1;
       if (c == 0 && j2 > 0) {
@@ -477,7 +495,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
       const int mode = tile_mode(j);
       j2 = j;
       auto run = [&](auto mode_c) {
-        sweep([&](const uint32_t (&v)[16], int c) { pass2_chunk(mode_c, v, c, j * kBN + kh + 16 * c); });
+        sweep([&](const uint32_t (&v)[16], int c) { pass2_chunk(mode_c, v, c, j * kBN + kh + 16 * c, 4 * j + c); });
       };
       if (mode == kFast) run(IntC<kFast>{});
       else if (mode == kLimited) run(IntC<kLimited>{});

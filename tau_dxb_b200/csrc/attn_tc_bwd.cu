@@ -469,9 +469,40 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     const bool has_mask = p.mask != nullptr || p.causal;
     float2 acc_tau = make_float2(0.f, 0.f), acc_alpha = make_float2(0.f, 0.f);
     int qs = 0, qph = 0;             // stage and phase of tile i in the Q / dO / statistics ring
-    auto chunk_math = [&](auto masked_c, auto full_c, const uint32_t (&rr)[32], int i, int col0,
-                          uint32_t (&pp)[8], uint32_t (&pf)[8]) {
+    // Clean chunks: where every x = alpha (s - m) of the chunk is above
+    // a2_clean / log2(e), none of the reference's clamps can act -- sigma and
+    // sigma^tau stay >= 1e-8 and sigma'/sigma (s - m) >= -30 (sigma'/sigma <= 1)
+    // -- so those chunks skip the three clamps. x_thr solves
+    // sigma(x_thr) = max(1e-8^(1/tau), 1e-8); the margin of 0.01 covers the
+    // polynomial and ex2 approximation errors.
+    float a2_clean = INFINITY;
+    if (SIG != TAU_DXB_SIGMA_RELU) {
+      const float pth = fmaxf(exp2f(kLog2Clamp / tau), 1e-8f);
+      const float x_thr = SIG == TAU_DXB_SIGMA_SOFTPLUS ? logf(expm1f(pth))
+                          : SIG == TAU_DXB_SIGMA_SIGMOID ? logf(pth / (1.f - pth)) : logf(pth);
+      a2_clean = kLog2e * fmaxf(x_thr + 0.01f, -29.9f * alpha);
+    }
+    // a2 = log2(e) alpha (s scale - m) of a 16-column chunk; true if the chunk is clean
+    auto chunk_a2 = [&](const uint32_t (&rr)[32], int col0, float2 (&a2v)[8]) -> bool {
+      const float* stc = stats + qs * 3 * kT;
+#pragma unroll
+      for (int e4 = 0; e4 < 16; e4 += 4) {
+        const float4 mc4 = *reinterpret_cast<const float4*>(stc + col0 + e4);
+        a2v[e4 >> 1] = tc::fma2(make_float2(__uint_as_float(rr[e4]), __uint_as_float(rr[e4 + 1])), sa2x2,
+                                make_float2(mc4.x, mc4.y));
+        a2v[(e4 >> 1) + 1] = tc::fma2(make_float2(__uint_as_float(rr[e4 + 2]), __uint_as_float(rr[e4 + 3])),
+                                      sa2x2, make_float2(mc4.z, mc4.w));
+      }
+      const float m0 = tc::min3(a2v[0].x, a2v[0].y, a2v[1].x), m1 = tc::min3(a2v[1].y, a2v[2].x, a2v[2].y);
+      const float m2 = tc::min3(a2v[3].x, a2v[3].y, a2v[4].x), m3 = tc::min3(a2v[4].y, a2v[5].x, a2v[5].y);
+      const float m4 = tc::min3(a2v[6].x, a2v[6].y, a2v[7].x);
+      const float amin = tc::min3(tc::min3(m0, m1, m2), tc::min3(m3, m4, a2v[7].y), INFINITY);
+      return __all_sync(0xffffffffu, amin >= a2_clean);
+    };
+    auto chunk_math = [&](auto masked_c, auto full_c, auto clean_c, const uint32_t (&rr)[32], int i, int col0,
+                          const float2 (&a2v)[8], uint32_t (&pp)[8], uint32_t (&pf)[8]) {
       constexpr bool kMasked = decltype(masked_c)::value, kFull = decltype(full_c)::value;
+      constexpr bool kClean = decltype(clean_c)::value;
       const float* stc = stats + qs * 3 * kT;
       float mv[kMasked ? 16 : 1];
       if constexpr (kMasked) {
@@ -483,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       }
 #pragma unroll
         for (int e4 = 0; e4 < 16; e4 += 4) {
-          const float4 mc4 = *reinterpret_cast<const float4*>(stc + col0 + e4);
+          const float4 mc4 = kMasked ? *reinterpret_cast<const float4*>(stc + col0 + e4) : make_float4(0.f, 0.f, 0.f, 0.f);
           const float4 rz4 = *reinterpret_cast<const float4*>(stc + kT + col0 + e4);
           const float4 dq4 = *reinterpret_cast<const float4*>(stc + 2 * kT + col0 + e4);
 #pragma unroll
@@ -492,10 +523,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
             const float2 mc = h2 ? make_float2(mc4.z, mc4.w) : make_float2(mc4.x, mc4.y);
             const float2 rz = h2 ? make_float2(rz4.z, rz4.w) : make_float2(rz4.x, rz4.y);
             const float2 dq = h2 ? make_float2(dq4.z, dq4.w) : make_float2(dq4.x, dq4.y);
-            float2 a2 = tc::fma2(make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), sa2x2, mc);
+            float2 a2;
             if constexpr (kMasked) {
+              a2 = tc::fma2(make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), sa2x2, mc);
               a2.x = fmaf(mv[e], al2, a2.x);
               a2.y = fmaf(mv[e + 1], al2, a2.y);
+            } else {
+              a2 = a2v[e >> 1];
             }
             float2 y, ratio;
             if (SIG == TAU_DXB_SIGMA_SOFTPLUS || SIG == TAU_DXB_SIGMA_SIGMOID) {
@@ -509,14 +543,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
               y = make_float2(ytau, ytau);
               ratio = make_float2(1.f, 1.f);
             }
-            float2 P = tc::mul2(make_float2(tc::ex2(fmaxf(y.x, ylo)), tc::ex2(fmaxf(y.y, ylo))), rz);
+            float2 P;
+            if constexpr (kClean) P = tc::mul2(make_float2(tc::ex2(y.x), tc::ex2(y.y)), rz);
+            else P = tc::mul2(make_float2(tc::ex2(fmaxf(y.x, ylo)), tc::ex2(fmaxf(y.y, ylo))), rz);
             if constexpr (!kFull) P = tc::mul2(P, kmask2);
             const float2 t = tc::mul2(P, tc::sub2(make_float2(__uint_as_float(rr[16 + e]),
                                                               __uint_as_float(rr[17 + e])), dq));
-            acc_tau = tc::fma2(t, make_float2(fmaxf(y.x, ytau), fmaxf(y.y, ytau)), acc_tau);
             // x = s - rowmax <= 0, so ratio * a2 <= 0: only the lower clip can act
             const float2 ra = tc::mul2(ratio, a2);
-            acc_alpha = tc::fma2(t, make_float2(fmaxf(ra.x, -glim), fmaxf(ra.y, -glim)), acc_alpha);
+            if constexpr (kClean) {
+              acc_tau = tc::fma2(t, y, acc_tau);
+              acc_alpha = tc::fma2(t, ra, acc_alpha);
+            } else {
+              acc_tau = tc::fma2(t, make_float2(fmaxf(y.x, ytau), fmaxf(y.y, ytau)), acc_tau);
+              acc_alpha = tc::fma2(t, make_float2(fmaxf(ra.x, -glim), fmaxf(ra.y, -glim)), acc_alpha);
+            }
             const float2 F = tc::mul2(t, ratio);
             pp[e >> 1] = tc::pack_bf16(P.x, P.y);
             pf[e >> 1] = tc::pack_bf16(F.x, F.y);
@@ -547,12 +588,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         uint32_t pp[8], pf[8];
         // branch-free bodies (mask / partial key tile decided per chunk) so the
         // scheduler can interleave the eight column pairs
+        float2 a2v[8];
         if (has_mask) {
-          if (tile_full) chunk_math(BoolC<true>{}, BoolC<true>{}, rr, i, col0, pp, pf);
-          else chunk_math(BoolC<true>{}, BoolC<false>{}, rr, i, col0, pp, pf);
+          if (tile_full) chunk_math(BoolC<true>{}, BoolC<true>{}, BoolC<false>{}, rr, i, col0, a2v, pp, pf);
+          else chunk_math(BoolC<true>{}, BoolC<false>{}, BoolC<false>{}, rr, i, col0, a2v, pp, pf);
+        } else if (chunk_a2(rr, col0, a2v)) {
+          if (tile_full) chunk_math(BoolC<false>{}, BoolC<true>{}, BoolC<true>{}, rr, i, col0, a2v, pp, pf);
+          else chunk_math(BoolC<false>{}, BoolC<false>{}, BoolC<true>{}, rr, i, col0, a2v, pp, pf);
         } else {
-          if (tile_full) chunk_math(BoolC<false>{}, BoolC<true>{}, rr, i, col0, pp, pf);
-          else chunk_math(BoolC<false>{}, BoolC<false>{}, rr, i, col0, pp, pf);
+          if (tile_full) chunk_math(BoolC<false>{}, BoolC<true>{}, BoolC<false>{}, rr, i, col0, a2v, pp, pf);
+          else chunk_math(BoolC<false>{}, BoolC<false>{}, BoolC<false>{}, rr, i, col0, a2v, pp, pf);
         }
         if (c == 0) {
           // P^T in TMEM is free once the previous tile's dV MMA is done, the dS^T

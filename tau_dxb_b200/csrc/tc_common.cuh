@@ -321,10 +321,22 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
                : "memory");
 }
 
+// three-input min (NaN operands are ignored, as by fminf)
+__device__ __forceinline__ float min3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 // three-input max (NaN operands are ignored, as by fmaxf)
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// 1.0f if a == b (ordered), else 0.0f
+__device__ __forceinline__ float eq_flag(float a, float b) {
+  float d;
+  asm("set.eq.f32.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
   return d;
 }
 // 0xFFFFFFFF if a == b (ordered), else 0
