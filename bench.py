@@ -52,8 +52,11 @@ def log(*a):
 
 # DRAM bytes per launch (read + write) of the main kernels at the encoder_self
 # workload (B=16), from one ncu capture each; traffic grows with B.
-BWD_MAIN_TRAFFIC = 360.6e6
-FWD_TRAFFIC = 131.5e6
+BWD_MAIN_TRAFFIC = 361.4e6
+FWD_TRAFFIC = 129.2e6
+# WTA forward (encoder, [24000, 3072]): DRAM reads 147.5 MB + writes 101.6 MB in
+# one capture; the writes still in L2 at kernel end are not counted there
+WTA_FWD_TRAFFIC = 249.1e6
 
 
 def sfu_floor(c, ms, clk, sms):
@@ -531,7 +534,9 @@ def run_ours(args, rank, world, local_rank):
             "bound": "hbm", "kernel": "wta_fwd16_kernel (encoder, k=306)",
             "achieved": result["wta"]["encoder_wta_k306"]["fwd_gbs"], "peak": load_peaks()[0],
             "unit": "GB/s", "frac": round(result["wta"]["encoder_wta_k306"]["fwd_gbs"] / load_peaks()[0], 4),
-            "traffic": None}
+            "traffic": WTA_FWD_TRAFFIC,
+            "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one launch (ncu); writes still "
+                            "in L2 when the kernel ends are not counted"}
     if rank == 0 and not args.no_cpu:
         result["cpu_baseline"] = cpu_baseline_sample(reps=8)
     return result
@@ -573,7 +578,16 @@ def run_reference(args, rank, world):
             "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def _emit(line: str, fd: int) -> None:
+    os.write(fd, (line + "\n").encode())
+
+
 def main():
+    # stdout carries exactly one JSON line: everything else that writes to file
+    # descriptor 1 (NCCL's version banner, library prints) goes to stderr
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
@@ -602,7 +616,7 @@ def main():
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
-            print(json.dumps(res), flush=True)
+            _emit(json.dumps(res), json_fd)
         return
     import torch
     import torch.distributed as dist
@@ -615,14 +629,14 @@ def main():
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
         if rank == 0:
-            print(json.dumps({"wta": wta_sub_bench(torch, device)}), flush=True)
+            _emit(json.dumps({"wta": wta_sub_bench(torch, device)}), json_fd)
         if world > 1:
             dist.destroy_process_group()
         return
     try:
         res = run_ours(args, rank, world, local_rank)
         if rank == 0 and res is not None:
-            print(json.dumps(res), flush=True)
+            _emit(json.dumps(res), json_fd)
     finally:
         if world > 1:
             dist.destroy_process_group()

@@ -130,6 +130,25 @@ def test_bf16_auto_path_vs_fp32_oracle(A, sigma, causal, Lq, Lk):
     assert_close(mine, ref, TOL_BF16, f"bf16 {sigma}")
 
 
+@pytest.mark.parametrize("sigma", ["softplus", "sigmoid", "exp"])
+def test_bf16_tensor_path_clamped_and_clean_chunks(A, sigma):
+    """Large alpha and tau and a wide score range: some 16-column chunks of the
+    backward have sigma, sigma^tau below 1e-8 or the +-30 clip active (every
+    clamp of the reference applied), others none (the clamp-free path)."""
+    g = torch.Generator().manual_seed(11)
+    B, H, L = 2, 4, 260
+    Q = (torch.randn(B, H, L, 64, generator=g) * 1.6).to(torch.bfloat16)
+    K = (torch.randn(B, H, L, 64, generator=g) * 1.6).to(torch.bfloat16)
+    V = torch.randn(B, H, L, 64, generator=g).to(torch.bfloat16)
+    dO = torch.randn(B, H, L, 64, generator=g).to(torch.bfloat16)
+    lt = torch.tensor([-1.0, 0.5, 2.0, 3.5])
+    la = torch.tensor([0.0, 1.0, 1.5, -0.4])
+    assert_no_near_ties(Q, K, 0.125)
+    mine = run_op(A, Q, K, V, lt, la, sigma, dO, None, 0.125, path="tensor")
+    ref = oracle(Q, K, V, lt, la, sigma, dO, None, 0.125)
+    assert_close(mine, ref, TOL_BF16, f"clamped/clean {sigma}")
+
+
 def test_tau1_exp_equals_softmax_on_gpu(A):
     Q, K, V, _, la, dO = make_inputs(2, 4, 100, 150, seed=4)
     lt = torch.full((4,), -30.0)
