@@ -430,13 +430,47 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
       }
       return tc::ex2(fmaxf(y, ylo));
     };
+    // q for a pair of scores on packed fp32 pairs (fast chunks)
+    float2 cyp[TAU_POLY_DEG + 1];
+    {
+      const float g0[] = TAU_POLY_G_COEFFS, h0[] = TAU_POLY_H_COEFFS;
+#pragma unroll
+      for (int u = 0; u <= TAU_POLY_DEG; ++u) {
+        const float yc = SIG == TAU_DXB_SIGMA_SIGMOID ? -tau * h0[u] : tau * g0[u];
+        cyp[u] = make_float2(yc, yc);
+      }
+    }
+    const float2 tau2 = make_float2(tau, tau), sa22 = make_float2(sa2, sa2), nma22 = make_float2(-ma2, -ma2);
+    auto qval2 = [&](float2 raw2) -> float2 {
+      const float2 a2 = tc::fma2(raw2, sa22, nma22);
+      float2 y;
+      if (SIG == TAU_DXB_SIGMA_SOFTPLUS || SIG == TAU_DXB_SIGMA_SIGMOID) {
+        const float2 ex = make_float2(tc::ex2(a2.x), tc::ex2(a2.y));
+        float2 acc = cyp[TAU_POLY_DEG];
+#pragma unroll
+        for (int u = TAU_POLY_DEG - 1; u >= 0; --u) acc = tc::fma2(acc, ex, cyp[u]);
+        y = tc::fma2(tau2, a2, acc);
+      } else if (SIG == TAU_DXB_SIGMA_EXP) {
+        y = tc::mul2(tau2, a2);
+      } else {
+        y = make_float2(ylo, ylo);
+      }
+      return make_float2(tc::ex2(fmaxf(y.x, ylo)), tc::ex2(fmaxf(y.y, ylo)));
+    };
     int j2 = 0;                    // key tile of the current pass-2 step
     auto pass2_chunk = [&](auto mode_c, const uint32_t (&v)[16], int c, int key0, int cid) {
       constexpr int kMode = decltype(mode_c)::value;
       uint32_t pk[8];
       uint32_t eq = 0;             // keys of this chunk whose score equals the max
+      float2 l2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int e = 0; e < 16; e += 2) {
+        if constexpr (kMode == kFast) {
+          const float2 q2 = qval2(make_float2(__uint_as_float(v[e]), __uint_as_float(v[e + 1])));
+          l2 = tc::add2(l2, q2);
+          pk[e >> 1] = tc::pack_bf16(q2.x, q2.y);
+          continue;
+        }
         float qq[2];
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -463,6 +497,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
         l1 += qq[1];
         pk[e >> 1] = tc::pack_bf16(qq[0], qq[1]);
       }
+      l0 += l2.x;
+      l1 += l2.y;
       if constexpr (kMode == kFast) {
         if (cid == mchunk) {             // the chunk that holds this half's first fast max
           // bit e of the sum = (raw_e == traw); 1.0 / 0.0 flags, FMA-pipe accumulation
