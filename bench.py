@@ -225,6 +225,35 @@ def attn_sub_bench(torch, c, seed, device, iters=10, warm=3):
     return out
 
 
+def decode_sub_bench(torch, device, iters=20, warm=3):
+    """KV-cached decoding: one query row per (b, h) against the cache, B=16 H=12
+    D=64 bf16 -- cross-attention over 1500 encoder frames (exp) and decoder
+    self-attention over 448 tokens (sigmoid, causal). GB/s on the K and V bytes
+    each call must read once (the roofline of the decode kernel)."""
+    out = {}
+    for name, sigma, Lk, causal in (("decoder_cross_decode", "exp", 1500, False),
+                                    ("decoder_self_decode", "sigmoid", 448, True)):
+        c = dict(name=name, sigma=sigma, B=16, H=12, Lq=1, Lk=Lk, D=64, scale=0.125, causal=causal)
+        # 8 independent caches in rotation so that the K/V bytes come from HBM
+        runners = [AttnRunner(torch, c, 50 + i, device) for i in range(8)]
+        cs = torch.cuda.current_stream()
+        sp = cs.cuda_stream
+        it = [0]
+
+        def fwd():
+            runners[it[0] % len(runners)].fwd(sp)
+            it[0] += 1
+        for _ in range(warm):
+            fwd()
+        t = time_events(torch, fwd, iters, cs)
+        nbytes = 16 * 12 * Lk * 64 * 2 * 2
+        out[name] = {"Lk": Lk, "sigma": sigma, "us": round(t * 1e3, 2), "kv_bytes": nbytes,
+                     "gbs": round(nbytes / (t * 1e-3) / 1e9, 1)}
+        del runners
+        torch.cuda.empty_cache()
+    return out
+
+
 def wta_sub_bench(torch, device, iters=20, warm=3):
     """WTA kernels: GB/s on algorithmic bytes (2 B read + 2 B y + 1/8 B mask per element)."""
     from tau_dxb_b200 import wta as W
@@ -529,6 +558,7 @@ def run_ours(args, rank, world, local_rank):
         if args.long:
             subs[LONG["name"]] = attn_sub_bench(torch, LONG, 8, device, iters=3, warm=1)
         result["attention_sites"] = subs
+        result["decode"] = decode_sub_bench(torch, device)
         result["wta"] = wta_sub_bench(torch, device)
         result["wta_roofline"] = {
             "bound": "hbm", "kernel": "wta_fwd16_kernel (encoder, k=306)",

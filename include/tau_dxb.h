@@ -52,7 +52,10 @@ extern "C" {
 #define TAU_DXB_SIGMA_RELU     3
 
 /* ---- attention kernel path ---------------------------------------------- */
-#define TAU_DXB_PATH_AUTO    0  /* tensor cores when supported, else precise */
+#define TAU_DXB_PATH_AUTO    0  /* forward with Lq <= 8 (KV-cached decoding):
+                                   one pass over K and V per query row, fp32
+                                   math; otherwise tensor cores when supported,
+                                   else precise */
 #define TAU_DXB_PATH_PRECISE 1  /* fp32 CUDA-core math and accumulation */
 #define TAU_DXB_PATH_TENSOR  2  /* tcgen05/TMEM + TMA; error if unsupported */
 

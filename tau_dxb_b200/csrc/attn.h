@@ -53,6 +53,12 @@ int* device_error_word();   // device address of the kernels' error word
 int attn_fwd_tensor(const AttnProblem& p, cudaStream_t st);
 int attn_bwd_tensor_main(const AttnProblem& p, cudaStream_t st);
 
+// decode forward for a few query rows (KV-cached decoding): one CTA per row,
+// one pass over K and V
+constexpr int kDecodeMaxRows = 8, kDecodeMaxKeys = 32768;
+bool attn_decode_supported(const AttnProblem& p);
+int attn_fwd_decode(const AttnProblem& p, cudaStream_t st);
+
 // shared backward stages
 int attn_bwd_prologue(const AttnProblem& p, cudaStream_t st);   // zero + rowsum(dO*O)
 int attn_bwd_epilogue(const AttnProblem& p, cudaStream_t st);   // argmax fix, scaled dQ/dK

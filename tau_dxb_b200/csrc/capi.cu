@@ -131,6 +131,8 @@ int tau_attn_fwd(const void* q, const int64_t q_stride[4], const void* k, const 
   p.row_max = row_max; p.row_z = row_z; p.row_argmax = row_argmax;
   if (B == 0 || Lq == 0) return TAU_DXB_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // a few query rows (KV-cached decoding): one pass over K and V per row
+  if (path == TAU_DXB_PATH_AUTO && attn_decode_supported(p)) return attn_fwd_decode(p, st);
   const bool tc = use_tensor(p, path, &rc, false);
   if (rc) return rc;
   return tc ? attn_fwd_tensor(p, st) : attn_fwd_precise(p, st);

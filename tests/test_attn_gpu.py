@@ -224,7 +224,7 @@ def fwd_direct(Q, K, V, lt, la, sigma, scale, path, mask=None, causal=False, lay
         C.SIGMA_IDS[sigma], float(scale), md.data_ptr() if md is not None else None,
         C.F32 if md is not None else 0, C.strides4(md) if md is not None else None, int(causal),
         out.data_ptr(), C.strides4(out), m.data_ptr(), z.data_ptr(), a.data_ptr(),
-        {"tensor": C.PATH_TENSOR, "precise": C.PATH_PRECISE}[path], C.stream_ptr())
+        {"tensor": C.PATH_TENSOR, "precise": C.PATH_PRECISE, "auto": C.PATH_AUTO}[path], C.stream_ptr())
     C.check("tau_attn_fwd", rc)
     torch.cuda.synchronize()
     assert C.lib().tau_dxb_device_error(1) == 0
@@ -283,3 +283,57 @@ def test_tensor_causal_flag_equals_mask(A):
     b = run_op(A, Q, K, V, lt, la, "sigmoid", dO, None, 0.125, path="tensor", causal_fn=True)
     for x, y in zip(a, b):
         assert rel_err(x, y) < 2e-3
+
+
+# ------------------------------------------------------------ decode forward (Lq <= 8)
+
+@pytest.mark.parametrize("sigma,causal,B,H,Lq,Lk", [
+    ("sigmoid", True, 2, 12, 1, 37),        # decoder self-attention, one new token
+    ("sigmoid", True, 2, 3, 1, 448),
+    ("exp", False, 2, 12, 1, 1500),         # cross-attention over the encoder frames
+    ("softplus", False, 1, 4, 3, 700),
+    ("softplus", False, 2, 2, 8, 64),
+    ("relu", False, 1, 2, 2, 50)])
+def test_decode_forward_vs_oracle(sigma, causal, B, H, Lq, Lk):
+    """A few query rows (KV-cached decoding) take the one-pass decode kernel on
+    the auto path; fp32 math, so the row state is held to the precise path's
+    tolerance and the bf16 output to its rounding."""
+    Q, K, V, lt, la, _ = make_inputs(B, H, Lq, Lk, seed=Lq * 31 + Lk, dtype=torch.bfloat16, la_std=0.3)
+    scale = 0.125
+    mask = torch.from_numpy(OA.causal_mask(Lq, Lk)) if causal else None
+    assert_no_near_ties(Q, K, scale, mask)
+    out, m, z, a = fwd_direct(Q, K, V, lt, la, sigma, scale, "auto", causal=causal)
+    f = lambda t: t.float().numpy()
+    ref_out, ctx = OA.forward(f(Q), f(K), f(V), f(lt), f(la), sigma,
+                              None if mask is None else mask.numpy(), scale)
+    assert rel_err(out, ref_out) < 8e-3, rel_err(out, ref_out)
+    assert np.abs(m - ctx["m"]).max() < 1e-5
+    assert np.array_equal(a, ctx["argmax"])
+    assert rel_err(z, ctx["Z"]) < TOL_FP32
+
+
+def test_decode_forward_mask_tensor_and_fallback():
+    """An explicit additive mask on the decode kernel; fp32 inputs (no 16-byte
+    rows of 8 halves) take the tiled precise kernel on the auto path."""
+    Q, K, V, lt, la, _ = make_inputs(2, 3, 2, 90, seed=5, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(5)
+    mask = torch.where(torch.rand(1, 1, 2, 90, generator=g) < 0.3, -1e9, 0.0)
+    out, m, z, a = fwd_direct(Q, K, V, lt, la, "softplus", 0.125, "auto", mask=mask)
+    f = lambda t: t.float().numpy()
+    ref_out, ctx = OA.forward(f(Q), f(K), f(V), f(lt), f(la), "softplus", mask.numpy(), 0.125)
+    assert rel_err(out, ref_out) < 8e-3
+    assert np.array_equal(a, ctx["argmax"]) and rel_err(z, ctx["Z"]) < TOL_FP32
+    Qf, Kf, Vf = Q.float(), K.float(), V.float()
+    out, m, z, a = fwd_direct(Qf, Kf, Vf, lt, la, "softplus", 0.125, "auto", layout="bhld")
+    ref_out, ctx = OA.forward(f(Qf), f(Kf), f(Vf), f(lt), f(la), "softplus", None, 0.125)
+    assert rel_err(out, ref_out) < TOL_FP32 and np.array_equal(a, ctx["argmax"])
+
+
+def test_decode_rows_through_autograd_fwd_bwd(A):
+    """One-row calls through STauOpusAttentionFunction: the decode forward's row
+    state feeds the backward."""
+    Q, K, V, lt, la, dO = make_inputs(2, 4, 1, 300, seed=8, dtype=torch.bfloat16, la_std=0.2)
+    assert_no_near_ties(Q, K, 0.125)
+    mine = run_op(A, Q, K, V, lt, la, "softplus", dO, None, 0.125, path="auto")
+    ref = oracle(Q, K, V, lt, la, "softplus", dO, None, 0.125)
+    assert_close(mine, ref, TOL_BF16, "decode fwd + bwd")
