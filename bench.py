@@ -170,14 +170,14 @@ class AttnRunner:
         self.st = {n: s(getattr(self, n)) for n in ("Q", "K", "V", "O", "dO", "dQ", "dK", "dV")}
         self.device = device
 
-    def fwd(self, stream):
+    def fwd(self, stream, path=None):
         c, C, st = self.c, self.C, self.st
         rc = C.lib().tau_attn_fwd(
             self.Q.data_ptr(), st["Q"], self.K.data_ptr(), st["K"], self.V.data_ptr(), st["V"],
             C.BF16, c["B"], c["H"], c["Lq"], c["Lk"], c["D"], self.tau.data_ptr(),
             self.alpha.data_ptr(), self.sig, c["scale"], None, 0, None, int(c["causal"]),
             self.O.data_ptr(), st["O"], self.m.data_ptr(), self.z.data_ptr(), self.a.data_ptr(),
-            C.PATH_AUTO, stream)
+            C.PATH_AUTO if path is None else path, stream)
         C.check("tau_attn_fwd", rc)
 
     def bwd(self, stream):
@@ -240,15 +240,20 @@ def decode_sub_bench(torch, device, iters=20, warm=3):
         sp = cs.cuda_stream
         it = [0]
 
-        def fwd():
-            runners[it[0] % len(runners)].fwd(sp)
+        def fwd(path=None):
+            runners[it[0] % len(runners)].fwd(sp, path)
             it[0] += 1
         for _ in range(warm):
             fwd()
         t = time_events(torch, fwd, iters, cs)
+        from tau_dxb_b200 import _capi as C
+        for _ in range(warm):
+            fwd(C.PATH_TENSOR)
+        t_tiled = time_events(torch, lambda: fwd(C.PATH_TENSOR), iters, cs)
         nbytes = 16 * 12 * Lk * 64 * 2 * 2
         out[name] = {"Lk": Lk, "sigma": sigma, "us": round(t * 1e3, 2), "kv_bytes": nbytes,
-                     "gbs": round(nbytes / (t * 1e-3) / 1e9, 1)}
+                     "gbs": round(nbytes / (t * 1e-3) / 1e9, 1),
+                     "tiled_tensor_path_us": round(t_tiled * 1e3, 2)}
         del runners
         torch.cuda.empty_cache()
     return out
