@@ -573,18 +573,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       if (!ok) break;
       tc::tc_fence_after();
       uint8_t* DSt = smem + kOffDS + s * 2 * kTile + (grp >> 1) * kTile;   // this group's 64-query atom
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      // chunk c = 16 query columns: S^T and dP^T from TMEM, the elementwise math,
+      // P^T back to TMEM and dS^T to shared memory. Chunk 1's TMEM loads are
+      // issued right after chunk 0's math, so their latency overlaps chunk 0's
+      // stores and the wait for the previous tile's MMAs.
+      uint32_t rr[32];       // [0,16) scores, [16,32) dP of 16 query columns
+      auto chunk = [&](int c) {
         const int col0 = grp * 32 + c * 16;
-        uint32_t rr[32];     // [0,16) scores, [16,32) dP of 16 query columns
-        tc::tmem_ld16(tmem + lane_base + kColS + col0, rr);
-        tc::tmem_ld16(tmem + lane_base + kColDP + col0, rr + 16);
-        tc::tmem_wait_ld_regs(rr);
-        if (c == 1) {        // every TMEM read of this tile is done
-          tc::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) tc::mbar_arrive(&bars->s_free);
-        }
         uint32_t pp[8], pf[8];
         // branch-free bodies (mask / partial key tile decided per chunk) so the
         // scheduler can interleave the eight column pairs
@@ -600,13 +595,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           else chunk_math(BoolC<false>{}, BoolC<false>{}, BoolC<false>{}, rr, i, col0, a2v, pp, pf);
         }
         if (c == 0) {
+          // chunk 1's columns in flight while chunk 0 is stored
+          tc::tmem_ld16(tmem + lane_base + kColS + col0 + 16, rr);
+          tc::tmem_ld16(tmem + lane_base + kColDP + col0 + 16, rr + 16);
           // P^T in TMEM is free once the previous tile's dV MMA is done, the dS^T
           // buffer once the MMAs of the tile two back are done with it
           bool fr = i == 0 || tc::mbar_wait(&bars->p_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutCompute);
           if (fr && i >= 2) fr = tc::mbar_wait(&bars->ds_free[s], ((i >> 1) - 1) & 1, abort_flag, p.err,
                                                kErrTimeoutCompute);
           ok = __all_sync(0xffffffffu, fr);
-          if (!ok) break;
           tc::tc_fence_after();
         }
         // P^T: 16 queries = 8 packed columns of this lane's TMEM row
@@ -614,11 +611,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         // dS^T row: key r, 16 queries = two 16-byte chunks of the 64-query atom
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const int chunk = (((grp & 1) * 4 + c * 2 + u) ^ (r & 7)) << 4;
-          *reinterpret_cast<uint4*>(DSt + r * 128 + chunk) =
+          const int ch = (((grp & 1) * 4 + c * 2 + u) ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(DSt + r * 128 + ch) =
               make_uint4(pf[4 * u], pf[4 * u + 1], pf[4 * u + 2], pf[4 * u + 3]);
         }
-      }
+      };
+      tc::tmem_ld16(tmem + lane_base + kColS + grp * 32, rr);
+      tc::tmem_ld16(tmem + lane_base + kColDP + grp * 32, rr + 16);
+      tc::tmem_wait_ld_regs(rr);
+      chunk(0);
+      tc::tmem_wait_ld_regs(rr);
+      // every TMEM read of this tile's S^T / dP^T is done
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars->s_free);
+      if (ok) chunk(1);
       if (!ok) break;
       tc::tmem_wait_st();
       tc::fence_async_smem();

@@ -141,7 +141,8 @@ class PaddedHeadLoss(torch.nn.Module):
         from transformers.models.whisper.modeling_whisper import shift_tokens_right
         cfg = self.whisper.config
         dec_in = shift_tokens_right(labels, cfg.pad_token_id, cfg.decoder_start_token_id)
-        h = self.whisper.model(input_features, decoder_input_ids=dec_in).last_hidden_state
+        # no KV cache in training (it would copy every decoder layer's keys and values)
+        h = self.whisper.model(input_features, decoder_input_ids=dec_in, use_cache=False).last_hidden_state
         w = self.whisper.proj_out.weight
         if self.pad:
             w = torch.nn.functional.pad(w, (0, 0, 0, self.pad))
