@@ -6,7 +6,11 @@ One optimiser step of echo/train_echo_opus1.py:405-434 on B200:
   and WTA / sparse_grad (24 FFNs), gradient all-reduce (NCCL, bucketed and
   overlapped with the backward by DistributedDataParallel), clip_grad_norm 1.0,
   AdamW with the reference's two parameter groups (base lr / tau lr for
-  log_tau and log_alpha, weight decay 0.01).
+  log_tau and log_alpha, weight decay 0.01), the LR schedule (linear warmup,
+  then cosine with warm restarts, echo/train_echo_opus1.py:230-244) and the
+  weight EMA (decay 0.999, echo/train_echo_opus1.py:199-213) as one
+  multi-tensor lerp. grad_accum micro-batches per optimiser step (the
+  reference's GRAD_ACCUM; 1 here by default).
 
 Data parallelism shards by batch: every rank holds a replica and its own
 16-sample batch; the all-reduce averages every gradient, log_tau, log_alpha
@@ -41,6 +45,11 @@ class StepConfig:
     sparsity_lambda: float = 0.01
     init_k_ratio: float = 0.4
     clip: float = 1.0
+    grad_accum: int = 1
+    ema_decay: float = 0.999        # 0 disables the EMA
+    warmup_steps: int = 100
+    t0_steps: int = 400
+    t_mult: int = 2
     encoder_layers: int = 12
     decoder_layers: int = 12
     d_model: int = 768
@@ -91,6 +100,42 @@ def build_model(cfg: StepConfig, device, tau_init=None):
                              init_k_ratio=cfg.init_k_ratio, track_wins=True)
     model.train()
     return model
+
+
+def lr_lambda(warmup_steps: int, t0_steps: int, t_mult: int):
+    """LR factor of the reference's schedule (echo/train_echo_opus1.py:230-244):
+    linear warmup over warmup_steps, then cosine annealing restarted after
+    t0_steps, t0_steps * t_mult, ... steps."""
+    def fn(step: int) -> float:
+        if step < warmup_steps:
+            return step / max(1, warmup_steps)
+        s, length = step - warmup_steps, t0_steps
+        while s >= length > 0:
+            s -= length
+            length *= t_mult
+        if length <= 0:
+            return 1.0
+        return 0.5 * (1.0 + math.cos(math.pi * s / length))
+    return fn
+
+
+class WeightEMA:
+    """Shadow copies of the trainable weights, shadow += (1 - decay) (w - shadow)
+    after every optimiser step (echo/train_echo_opus1.py:199-213) -- one
+    multi-tensor lerp over all of them instead of a per-parameter loop."""
+
+    def __init__(self, model, decay: float):
+        self.decay = decay
+        self.names = [n for n, p in model.named_parameters() if p.requires_grad]
+        self.params = [p for p in model.parameters() if p.requires_grad]
+        self.shadow = [p.detach().clone() for p in self.params]
+
+    @torch.no_grad()
+    def update(self):
+        torch._foreach_lerp_(self.shadow, [p.detach() for p in self.params], 1.0 - self.decay)
+
+    def state_dict(self):
+        return dict(zip(self.names, self.shadow))
 
 
 def make_optimizer(model, cfg: StepConfig):
@@ -165,7 +210,11 @@ class TrainStep:
                            bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True,
                            broadcast_buffers=False)
         self.opt = make_optimizer(self.model, cfg)
+        self.sched = torch.optim.lr_scheduler.LambdaLR(
+            self.opt, lr_lambda=lr_lambda(cfg.warmup_steps, cfg.t0_steps, cfg.t_mult))
+        self.ema = WeightEMA(self.model, cfg.ema_decay) if cfg.ema_decay > 0 else None
         self.skipped = 0
+        self.micro = 0                  # micro-batches since the last optimiser step
 
     def loss(self, mel, labels):
         amp = torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.device.type == "cuda")
@@ -175,19 +224,31 @@ class TrainStep:
             return ce + self.cfg.sparsity_lambda * sp, ce
 
     def step(self, mel, labels):
-        """Forward, backward (+ all-reduce), clip, AdamW. Returns the loss tensor."""
-        loss, ce = self.loss(mel, labels)
-        loss.backward()
+        """One micro-batch: forward, backward (+ all-reduce); every grad_accum
+        micro-batches clip, AdamW, LR schedule and EMA. Returns the loss."""
+        import contextlib
+        accumulate = self.world > 1 and self.micro + 1 < self.cfg.grad_accum
+        with self.net.no_sync() if accumulate else contextlib.nullcontext():   # all-reduce on the last
+            loss, ce = self.loss(mel, labels)
+            (loss / self.cfg.grad_accum).backward()
         bad = (~torch.isfinite(loss.detach())).float().reshape(1)
         if self.world > 1:
             dist.all_reduce(bad)
         if float(bad.item()) > 0:       # every rank skips together
             self.opt.zero_grad(set_to_none=True)
+            self.micro = 0
             self.skipped += 1
             return loss.detach()
+        self.micro += 1
+        if self.micro < self.cfg.grad_accum:
+            return loss.detach()
+        self.micro = 0
         torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.clip)
         self.opt.step()
+        self.sched.step()
         self.opt.zero_grad(set_to_none=True)
+        if self.ema is not None:
+            self.ema.update()
         return loss.detach()
 
 

@@ -1,11 +1,13 @@
 """Generate the golden vectors in this directory by running the REFERENCE.
 
 Run once in a container that has the reference checkout (it reads
-echo/stau_opus_operator.py, echo/triton_wta.py and
-echo/patch_whisper_sparse_grad.py from it); the resulting .npz files are
-committed, so tests never need the reference at run time.
+echo/stau_opus_operator.py, echo/triton_wta.py,
+echo/patch_whisper_sparse_grad.py and the LR lambda of
+echo/train_echo_opus1.py from it); the resulting .npz files are committed, so
+tests never need the reference at run time.
 
     python tests/golden/make_golden.py [/path/to/reference]
+    TAU_DXB_GOLDEN_ONLY=lr_table python tests/golden/make_golden.py   # one table
 
 Every case is seeded; attention inputs and the reference's outputs are
 stored in fp32, WTA inputs/outputs as raw bf16 bit patterns (uint16) and
@@ -135,13 +137,41 @@ def make_k_table(ref):
     print("wrote k_table")
 
 
+def make_lr_table(ref):
+    """The reference's LR lambda (echo/train_echo_opus1.py:230-244): its
+    source is taken from the training script and executed alone (the script's
+    top level needs the training data)."""
+    import ast
+    import math
+    path = os.path.join(ref, "echo", "train_echo_opus1.py")
+    tree = ast.parse(open(path).read())
+    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "make_lr_lambda")
+    ns = {"math": math}
+    exec(compile(ast.Module(body=[fn], type_ignores=[]), path, "exec"), ns)
+    rows = []
+    for warm, t0, tm in ((0, 10, 2), (5, 12, 2), (100, 400, 2), (7, 3, 1), (1, 1, 3)):
+        f = ns["make_lr_lambda"](warm, t0, tm)
+        for step in range(0, 4000, 7):
+            rows.append((warm, t0, tm, step, f(step)))
+    a = np.array(rows, dtype=np.float64)
+    np.savez_compressed(os.path.join(HERE, "lr_table.npz"), warmup=a[:, 0].astype(np.int64),
+                        t0=a[:, 1].astype(np.int64), t_mult=a[:, 2].astype(np.int64),
+                        step=a[:, 3].astype(np.int64), factor=a[:, 4])
+    print("wrote lr_table")
+
+
 def main(argv):
     ref = _ref_path(argv)
     sys.path.insert(0, os.path.join(ref, "echo"))
     torch.set_num_threads(4)
+    only = os.environ.get("TAU_DXB_GOLDEN_ONLY")
+    if only:
+        globals()["make_" + only](ref)
+        return
     make_attn(ref)
     make_wta(ref)
     make_k_table(ref)
+    make_lr_table(ref)
 
 
 if __name__ == "__main__":

@@ -8,6 +8,7 @@ import json
 import math
 
 import pytest
+import numpy as np
 import torch
 
 from oracle_ops import use_oracle_ops
@@ -178,3 +179,44 @@ def test_padded_head_loss_equals_the_plain_head():
     for n, p in model.named_parameters():
         if n in g_ref:
             assert torch.allclose(p.grad, g_ref[n], rtol=1e-10, atol=1e-12), n
+
+
+def test_lr_schedule_matches_reference_table():
+    """Warmup + cosine warm restarts, against the reference's own lambda."""
+    import os
+    from conftest import GOLDEN
+    from tau_dxb_b200 import train as T
+    z = np.load(os.path.join(GOLDEN, "lr_table.npz"))
+    for w, t0, tm, step, f in zip(z["warmup"], z["t0"], z["t_mult"], z["step"], z["factor"]):
+        assert abs(T.lr_lambda(int(w), int(t0), int(tm))(int(step)) - float(f)) < 1e-12, (w, t0, tm, step)
+
+
+def test_train_step_ema_schedule_and_accumulation(monkeypatch):
+    """grad_accum micro-batches make one optimiser step; the LR schedule steps
+    with it and the EMA shadow moves by (1 - decay) toward the new weights."""
+    from tau_dxb_b200 import train as T
+    use_oracle_ops(monkeypatch)
+    cfg = T.StepConfig(batch=1, frames=200, label_len=16, min_label=6, encoder_layers=1,
+                       decoder_layers=1, d_model=64, heads=2, ffn=128, vocab=300, grad_accum=2,
+                       ema_decay=0.9, warmup_steps=4, t0_steps=8, lr=1e-3)
+    step = T.TrainStep(cfg, "cpu")
+    g = torch.Generator().manual_seed(4)
+    b = [T.synthetic_batch(cfg, "cpu", g) for _ in range(2)]
+    w0 = [p.detach().clone() for p in step.model.parameters()]
+    step.step(*b[0])
+    assert all(torch.equal(a, p.detach()) for a, p in zip(w0, step.model.parameters()))
+    assert step.sched.last_epoch == 0 and step.micro == 1
+    step.step(*b[1])
+    assert step.sched.last_epoch == 1 and step.micro == 0
+    # the first optimiser step runs at warmup factor 0 (as in the reference)
+    assert all(torch.equal(a, p.detach()) for a, p in zip(w0, step.model.parameters()))
+    assert step.opt.param_groups[0]["lr"] == pytest.approx(1e-3 * T.lr_lambda(4, 8, 2)(1))
+    shadow1 = [t.clone() for t in step.ema.shadow]
+    step.step(*b[0])
+    step.step(*b[1])
+    params = [p for p in step.model.parameters() if p.requires_grad]
+    moved = 0
+    for p, s0, s1 in zip(params, shadow1, step.ema.shadow):
+        assert torch.allclose(s1, s0 + 0.1 * (p.detach() - s0), atol=1e-7)
+        moved += int(not torch.equal(s1, s0))
+    assert moved > 0
