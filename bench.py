@@ -259,6 +259,32 @@ def decode_sub_bench(torch, device, iters=20, warm=3):
     return out
 
 
+def features_sub_bench(torch, device, iters=10, warm=3):
+    """Whisper log-mel features of 16 x 30 s of audio on the GPU, against the
+    host extractor the reference's dataset calls per sample (one sample timed)."""
+    import numpy as np
+    from tau_dxb_b200 import features as Fe
+    g = torch.Generator(device=device).manual_seed(3)
+    x = torch.randn(16, Fe.N_SAMPLES, device=device, generator=g) * 0.1
+    for _ in range(warm):
+        Fe.log_mel_spectrogram(x)
+    cs = torch.cuda.current_stream()
+    t = time_events(torch, lambda: Fe.log_mel_spectrogram(x), iters, cs)
+    out = {"batch": 16, "seconds_each": 30, "gpu_ms": round(t, 4), "gpu_samples_per_s": round(16 / (t * 1e-3), 1)}
+    try:
+        from transformers import WhisperFeatureExtractor
+        fe = WhisperFeatureExtractor()
+        a = x[0].cpu().numpy()
+        fe(a, sampling_rate=16000, return_tensors="np")
+        t0 = time.perf_counter()
+        fe(a, sampling_rate=16000, return_tensors="np")
+        cpu_s = time.perf_counter() - t0
+        out["host_extractor_ms_per_sample"] = round(cpu_s * 1e3, 2)
+    except Exception as e:  # transformers missing: report the GPU side only
+        out["host_extractor"] = f"unavailable: {type(e).__name__}"
+    return out
+
+
 def wta_sub_bench(torch, device, iters=20, warm=3):
     """WTA kernels: GB/s on algorithmic bytes (2 B read + 2 B y + 1/8 B mask per element)."""
     from tau_dxb_b200 import wta as W
@@ -564,6 +590,7 @@ def run_ours(args, rank, world, local_rank):
             subs[LONG["name"]] = attn_sub_bench(torch, LONG, 8, device, iters=3, warm=1)
         result["attention_sites"] = subs
         result["decode"] = decode_sub_bench(torch, device)
+        result["features"] = features_sub_bench(torch, device)
         result["wta"] = wta_sub_bench(torch, device)
         result["wta_roofline"] = {
             "bound": "hbm", "kernel": "wta_fwd16_kernel (encoder, k=306)",

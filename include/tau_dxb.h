@@ -218,6 +218,25 @@ TAU_DXB_API int wta_bwd(const void* dy, int32_t dtype, const uint8_t* bitmask,
 TAU_DXB_API int wta_k_from_logits(const float* logits, int64_t n, int64_t d_ff, int32_t* k_out,
                       void* stream);
 
+/*
+ * Whisper log-mel features of a batch of waveforms on the GPU.
+ * Replaces the per-sample host call processor.feature_extractor(audio,
+ * sampling_rate=16000) of the reference's dataset (echo/train_echo_opus1.py:126),
+ * i.e. WhisperFeatureExtractor: centred 400-sample frames every 160 samples
+ * (reflect padding), periodic Hann window, power spectrum, mel filter bank,
+ * log10(max(mel, 1e-10)), then per sample max(x, max - 8) and (x + 4) / 4.
+ *
+ * audio: fp32 [batch, n_samples], 16 kHz, n_samples a multiple of 160 and
+ *        >= 400 (480000 = 30 s for Whisper; pad or truncate before the call).
+ * mel_filters: fp32 [201][80] (row = frequency bin), the extractor's mel_filters.
+ * out: fp32 [batch, 80, n_samples / 160].
+ * workspace: device memory of whisper_log_mel_workspace_bytes(batch) bytes.
+ */
+TAU_DXB_API size_t whisper_log_mel_workspace_bytes(int64_t batch);
+TAU_DXB_API int whisper_log_mel(const float* audio, int64_t batch, int64_t n_samples,
+                                const float* mel_filters, float* out, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -45,6 +45,8 @@ SIGNATURES = {
         _vp, _vp, _vp,                                # row_max, row_z, row_argmax
         _i32, _vp]),                                  # path, stream
     "tau_attn_bwd_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, _i64]),
+    "whisper_log_mel_workspace_bytes": (ctypes.c_size_t, [_i64]),
+    "whisper_log_mel": (ctypes.c_int, [_vp, _i64, _i64, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "tau_attn_bwd": (ctypes.c_int, [
         _vp, _i64p, _vp, _i64p, _vp, _i64p,           # q, k, v
         _vp, _i64p, _vp, _i64p,                       # out, dout

@@ -50,6 +50,8 @@ int wta_fwd_impl(const void*, int32_t, int64_t, int64_t, int64_t, int64_t, const
                  void*, uint8_t*, int32_t*, cudaStream_t);
 int wta_bwd_impl(const void*, int32_t, const uint8_t*, int64_t, int64_t, void*, cudaStream_t);
 int wta_k_from_logits_impl(const float*, int64_t, int64_t, int32_t*, cudaStream_t);
+size_t whisper_log_mel_workspace(int64_t batch);
+int whisper_log_mel_impl(const float*, int64_t, int64_t, const float*, float*, void*, size_t, cudaStream_t);
 
 namespace {
 
@@ -217,6 +219,17 @@ int wta_bwd(const void* dy, int32_t dtype, const uint8_t* bitmask, int64_t n_row
 int wta_k_from_logits(const float* logits, int64_t n, int64_t d_ff, int32_t* k_out, void* stream) {
   g_last_error[0] = 0;
   return wta_k_from_logits_impl(logits, n, d_ff, k_out, static_cast<cudaStream_t>(stream));
+}
+
+size_t whisper_log_mel_workspace_bytes(int64_t batch) {
+  return batch < 0 ? 0 : whisper_log_mel_workspace(batch);
+}
+
+int whisper_log_mel(const float* audio, int64_t batch, int64_t n_samples, const float* mel_filters,
+                    float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error[0] = 0;
+  return whisper_log_mel_impl(audio, batch, n_samples, mel_filters, out, workspace, workspace_bytes,
+                              static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
