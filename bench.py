@@ -285,6 +285,44 @@ def features_sub_bench(torch, device, iters=10, warm=3):
     return out
 
 
+def tau_star_sub_bench(torch, device, iters=5, warm=3, cpu_rows=96):
+    """tau* of one Whisper-small encoder self-attention call as the reference's
+    estimator runs it (12 heads x 1500 query rows x 1500 keys, softplus,
+    n_iter = 100): device time of tau_star_solve over all 18000 rows, its
+    exp rate against the SFU ceiling (each Newton step takes one expf per
+    key), and the numpy oracle on a bounded sample of rows on the host."""
+    import numpy as np
+    from tau_dxb_b200 import tau_star as TS
+    g = torch.Generator(device=device).manual_seed(21)
+    # 4 score tensors in rotation: 432 MB, larger than L2
+    xs = [torch.randn(1, 12, 1500, 1500, device=device, generator=g) * 2.5 for _ in range(4)]
+    it = [0]
+
+    def run():
+        TS.solve_tau_star(xs[it[0] % 4], "softplus", n_iter=100)
+        it[0] += 1
+    for _ in range(warm):
+        run()
+    cs = torch.cuda.current_stream()
+    t = time_events(torch, run, iters, cs)
+    rows, T, n_iter = 12 * 1500, 1500, 100
+    exps = rows * T * (n_iter + 4)
+    out = {"workload": "encoder self-attention scores 12 x 1500 x 1500 fp32, softplus, n_iter 100",
+           "gpu_ms": round(t, 4), "rows_per_s": round(rows / (t * 1e-3), 1),
+           "gexp_per_s": round(exps / (t * 1e-3) / 1e9, 1), "scores_bytes": rows * T * 4}
+    from oracle import tau_star as OT
+    sample = xs[0].view(-1, T)[:cpu_rows].cpu().numpy()
+    OT.solve_tau_star(sample[:8], "softplus", n_iter=100)
+    t0 = time.perf_counter()
+    OT.solve_tau_star(sample, "softplus", n_iter=100)
+    cpu_s = time.perf_counter() - t0
+    out["cpu_baseline"] = {"kind": "port", "cores": 1, "sample": f"{cpu_rows} of the 18000 rows (numpy oracle)",
+                           "rows_per_s": round(cpu_rows / cpu_s, 1)}
+    del xs
+    torch.cuda.empty_cache()
+    return out
+
+
 def wta_sub_bench(torch, device, iters=20, warm=3):
     """WTA kernels: GB/s on algorithmic bytes (2 B read + 2 B y + 1/8 B mask per element)."""
     from tau_dxb_b200 import wta as W
@@ -591,6 +629,7 @@ def run_ours(args, rank, world, local_rank):
         result["attention_sites"] = subs
         result["decode"] = decode_sub_bench(torch, device)
         result["features"] = features_sub_bench(torch, device)
+        result["tau_star"] = tau_star_sub_bench(torch, device)
         result["wta"] = wta_sub_bench(torch, device)
         result["wta_roofline"] = {
             "bound": "hbm", "kernel": "wta_fwd16_kernel (encoder, k=306)",
@@ -664,6 +703,8 @@ def main():
                     help="headline kernels only, at this batch size (small cases for ncu captures)")
     ap.add_argument("--wta-only", action="store_true",
                     help="only the WTA sub-benchmark (JSON of its results; for ncu captures)")
+    ap.add_argument("--tau-star-only", action="store_true",
+                    help="only the tau* solver sub-benchmark (JSON of its results; for ncu captures)")
     args = ap.parse_args()
     if args.profile_batch:
         args.quick = args.no_e2e = args.no_cpu = args.no_train = True
@@ -687,11 +728,13 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
-    if args.wta_only:
+    if args.wta_only or args.tau_star_only:
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
         if rank == 0:
-            _emit(json.dumps({"wta": wta_sub_bench(torch, device)}), json_fd)
+            res = {"wta": wta_sub_bench(torch, device)} if args.wta_only else \
+                {"tau_star": tau_star_sub_bench(torch, device)}
+            _emit(json.dumps(res), json_fd)
         if world > 1:
             dist.destroy_process_group()
         return

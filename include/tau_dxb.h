@@ -51,6 +51,9 @@ extern "C" {
 #define TAU_DXB_SIGMA_EXP      2
 #define TAU_DXB_SIGMA_RELU     3
 
+/* ---- longest score row tau_star_solve accepts --------------------------- */
+#define TAU_DXB_TAU_STAR_MAX_KEYS 28672
+
 /* ---- attention kernel path ---------------------------------------------- */
 #define TAU_DXB_PATH_AUTO    0  /* forward with Lq <= 8 (KV-cached decoding):
                                    one pass over K and V per query row, fp32
@@ -236,6 +239,36 @@ TAU_DXB_API size_t whisper_log_mel_workspace_bytes(int64_t batch);
 TAU_DXB_API int whisper_log_mel(const float* audio, int64_t batch, int64_t n_samples,
                                 const float* mel_filters, float* out, void* workspace,
                                 size_t workspace_bytes, void* stream);
+
+/*
+ * tau* per score row: the batched Newton solver for
+ *   tau* = argmin_tau KL(softmax(s) || softmax(tau * log sigma(s))).
+ * Replaces solve_tau_star (tau_star/tau_star_solver.py:60-128), as
+ * estimate_tau_per_head calls it (tau_star/compute_tau_star_echo.py:116-136,
+ * n_iter = 100), with every Newton step of a row fused on chip.
+ *
+ * scores: fp32 [n_rows, T] with row stride row_stride (elements), T in
+ *         [1, TAU_DXB_TAU_STAR_MAX_KEYS]; masked keys may hold any finite
+ *         value or -inf, as in the reference.
+ * sigma: TAU_DXB_SIGMA_*; n_iter >= 0 Newton steps from tau_init, each
+ *        clamped to [tau_min, tau_max]; eps damps zero variance.
+ * tau_out, kl_out: fp32 [n_rows]; T == 1 gives (tau_init, 0); non-finite
+ *        results become tau_init and 0, as in the reference.
+ */
+TAU_DXB_API int tau_star_solve(const float* scores, int64_t n_rows, int64_t T, int64_t row_stride,
+                               int32_t sigma, int32_t n_iter, float tau_init, float tau_min,
+                               float tau_max, float eps, float* tau_out, float* kl_out,
+                               void* stream);
+
+/*
+ * One-shot tau estimate per score row, the Newton solver's warm start:
+ *   tau = clamp(Cov_ref(s, log sigma(s)) / (Var_ref(log sigma(s)) + 1e-6), 0.1, 10)
+ * under ref = softmax(s). Replaces solve_tau_star_analytic
+ * (tau_star/tau_star_solver.py:131-151). scores as tau_star_solve (any T >= 1);
+ * tau_out: fp32 [n_rows]. A NaN result is kept, as in the reference.
+ */
+TAU_DXB_API int tau_star_analytic(const float* scores, int64_t n_rows, int64_t T, int64_t row_stride,
+                                  int32_t sigma, float* tau_out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -52,6 +52,9 @@ int wta_bwd_impl(const void*, int32_t, const uint8_t*, int64_t, int64_t, void*, 
 int wta_k_from_logits_impl(const float*, int64_t, int64_t, int32_t*, cudaStream_t);
 size_t whisper_log_mel_workspace(int64_t batch);
 int whisper_log_mel_impl(const float*, int64_t, int64_t, const float*, float*, void*, size_t, cudaStream_t);
+int tau_star_solve_impl(const float*, int64_t, int64_t, int64_t, int32_t, int32_t, float, float, float, float,
+                        float*, float*, cudaStream_t);
+int tau_star_analytic_impl(const float*, int64_t, int64_t, int64_t, int32_t, float*, cudaStream_t);
 
 namespace {
 
@@ -230,6 +233,20 @@ int whisper_log_mel(const float* audio, int64_t batch, int64_t n_samples, const 
   g_last_error[0] = 0;
   return whisper_log_mel_impl(audio, batch, n_samples, mel_filters, out, workspace, workspace_bytes,
                               static_cast<cudaStream_t>(stream));
+}
+
+int tau_star_solve(const float* scores, int64_t n_rows, int64_t T, int64_t row_stride, int32_t sigma,
+                   int32_t n_iter, float tau_init, float tau_min, float tau_max, float eps, float* tau_out,
+                   float* kl_out, void* stream) {
+  g_last_error[0] = 0;
+  return tau_star_solve_impl(scores, n_rows, T, row_stride, sigma, n_iter, tau_init, tau_min, tau_max, eps,
+                             tau_out, kl_out, static_cast<cudaStream_t>(stream));
+}
+
+int tau_star_analytic(const float* scores, int64_t n_rows, int64_t T, int64_t row_stride, int32_t sigma,
+                      float* tau_out, void* stream) {
+  g_last_error[0] = 0;
+  return tau_star_analytic_impl(scores, n_rows, T, row_stride, sigma, tau_out, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -15,6 +15,7 @@ masks as little-endian packed bits.
 """
 from __future__ import annotations
 
+import json
 import os
 import sys
 
@@ -160,6 +161,52 @@ def make_lr_table(ref):
     print("wrote lr_table")
 
 
+def make_tau_star(ref):
+    """solve_tau_star of tau_star/tau_star_solver.py:60-128 (imported from the
+    reference) on seeded score rows, every sigma, with -1e9 key padding as its
+    estimator adds."""
+    sys.path.insert(0, os.path.join(ref, "tau_star"))
+    import tau_star_solver as TS
+    out = {}
+    cases = [("softplus", 57, 30, 2.0, 1.5), ("sigmoid", 300, 30, 2.0, 2.0), ("exp", 120, 100, 1.0, 3.0),
+             ("relu", 40, 20, 2.0, 1.0), ("softplus", 1, 30, 2.0, 1.0), ("softplus", 2, 50, 0.5, 4.0)]
+    for ci, (sig, T, n_iter, tau_init, spread) in enumerate(cases):
+        g = torch.Generator().manual_seed(500 + ci)
+        scores = torch.randn(24, T, generator=g) * spread
+        if T > 8:
+            scores[3, T - 5:] = -1e9            # padded keys
+        tau, kl = TS.solve_tau_star(scores, sigma=sig, n_iter=n_iter, tau_init=tau_init)
+        key = f"c{ci}"
+        out[key + "_scores"] = scores.numpy()
+        out[key + "_tau"] = tau.numpy()
+        out[key + "_kl"] = kl.numpy()
+        out[key + "_meta"] = np.array([T, n_iter, tau_init])
+        out[key + "_sigma"] = np.array(sig)
+        # one-shot estimate cov_ref(s, ls) / var_ref(ls) (tau_star_solver.py:131-151)
+        out[key + "_analytic"] = TS.solve_tau_star_analytic(scores, sigma=sig).numpy()
+    # TauStarEstimator (tau_star_solver.py:180-275): two modules, calls of
+    # different key lengths (padded with -1e9 to the longest), aggregated on the
+    # host; per-"head" entries are tau[h].mean() over the flattened (N, H) rows
+    est = TS.TauStarEstimator(n_iter=25)
+    g = torch.Generator().manual_seed(640)
+    calls = [("model.encoder.layers.0.self_attn", (2, 4, 6, 40)),
+             ("model.encoder.layers.0.self_attn", (1, 4, 5, 33)),
+             ("model.decoder.layers.1.encoder_attn", (3, 4, 2, 50)),
+             ("model.decoder.layers.1.encoder_attn", (2, 4, 3, 50))]
+    for ci, (name, shape) in enumerate(calls):
+        sc = torch.randn(*shape, generator=g) * 2.0
+        est.collect(name, sc)
+        out[f"e{ci}_scores"] = sc.numpy()
+        out[f"e{ci}_name"] = np.array(name)
+    for mi, r in enumerate(est.aggregate(device="cpu")):
+        out[f"m{mi}_name"] = np.array(r.module_name)
+        out[f"m{mi}_tau"] = np.array(r.tau_per_head)
+        out[f"m{mi}_kl"] = np.array(r.kl_per_head)
+        out[f"m{mi}_dict"] = np.array(json.dumps(r.to_dict()))
+    np.savez_compressed(os.path.join(HERE, "tau_star.npz"), **out)
+    print("wrote tau_star")
+
+
 def main(argv):
     ref = _ref_path(argv)
     sys.path.insert(0, os.path.join(ref, "echo"))
@@ -172,6 +219,7 @@ def main(argv):
     make_wta(ref)
     make_k_table(ref)
     make_lr_table(ref)
+    make_tau_star(ref)
 
 
 if __name__ == "__main__":

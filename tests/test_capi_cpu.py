@@ -24,7 +24,7 @@ def test_header_declares_expected_entry_points():
     names = _declared_functions()
     for n in ("tau_attn_fwd", "tau_attn_bwd", "tau_attn_bwd_workspace_bytes", "wta_fwd",
               "wta_bwd", "wta_k_from_logits", "tau_dxb_strerror", "tau_dxb_last_error",
-              "tau_dxb_version"):
+              "tau_dxb_version", "whisper_log_mel", "tau_star_solve", "tau_star_analytic"):
         assert n in names
 
 
@@ -57,6 +57,22 @@ def test_validation_without_gpu(C):
     rc = lib.tau_attn_fwd(None, s, None, s, None, s, 1, 1, 1, 8, 8, 64, None, None, 0, 1.0,
                           None, 0, None, 0, None, s, None, None, None, 0, None)
     assert rc == C.ERR_INVALID_ARGUMENT
+    # tau* solver: key count, sigma id and pointers are checked first
+    assert lib.tau_star_solve(None, 4, 0, 0, 0, 30, 2.0, 0.1, 10.0, 1e-6, None, None, None) == \
+        C.ERR_INVALID_ARGUMENT
+    assert lib.tau_star_solve(None, 4, C.TAU_STAR_MAX_KEYS + 1, C.TAU_STAR_MAX_KEYS + 1, 0, 30, 2.0, 0.1,
+                              10.0, 1e-6, None, None, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_star_solve(None, 4, 64, 64, 7, 30, 2.0, 0.1, 10.0, 1e-6, None, None, None) == \
+        C.ERR_INVALID_ARGUMENT
+    assert lib.tau_star_solve(None, 4, 64, 32, 0, 30, 2.0, 0.1, 10.0, 1e-6, None, None, None) == \
+        C.ERR_INVALID_ARGUMENT
+    assert lib.tau_star_solve(None, 4, 64, 64, 0, 30, 2.0, 0.1, 10.0, 1e-6, None, None, None) == \
+        C.ERR_INVALID_ARGUMENT
+    assert "null pointer" in C.last_error()
+    assert lib.tau_star_solve(None, 0, 64, 64, 0, 30, 2.0, 0.1, 10.0, 1e-6, None, None, None) == C.OK
+    assert lib.tau_star_analytic(None, 4, 64, 64, 9, None, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_star_analytic(None, 4, 64, 64, 0, None, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_star_analytic(None, 0, 64, 64, 0, None, None) == C.OK
 
 
 def test_workspace_size_formula(C):

@@ -125,3 +125,17 @@ def test_bf16_roundtrip():
     back = OW.bf16_bits_to_f32(bits)
     assert np.abs(back - v).max() <= np.abs(v).max() * 2 ** -8
     assert np.array_equal(OW.f32_to_bf16_bits(back), bits)
+
+
+def test_tau_star_oracle_matches_reference_golden():
+    from oracle import tau_star as OT
+    z = np.load(os.path.join(GOLDEN, "tau_star.npz"))
+    for ci in range(6):
+        k = f"c{ci}"
+        T, n_iter, tau_init = z[k + "_meta"]
+        tau, kl = OT.solve_tau_star(z[k + "_scores"], str(z[k + "_sigma"]), int(n_iter), float(tau_init))
+        # two keys: the KL is flat in tau near its minimum, so fp32 rounding moves
+        # tau by ~1e-3 while the KL agrees to 2e-7
+        rtol = 2e-3 if T <= 2 else 2e-5
+        assert np.allclose(tau, z[k + "_tau"], rtol=rtol, atol=2e-5), (ci, np.abs(tau - z[k + "_tau"]).max())
+        assert np.allclose(kl, z[k + "_kl"], rtol=1e-3, atol=2e-6), (ci, np.abs(kl - z[k + "_kl"]).max())
