@@ -406,7 +406,9 @@ def train_sub_bench(torch, device, world, rank, steps=10, warmup=3):
     e = torch.cuda.Event(enable_timing=True)
     s.record()
     for i in range(steps):
+        torch.cuda.nvtx.range_push("train_step")    # lets a profiler take the timed steps only
         step.step(*batches[i % 2])
+        torch.cuda.nvtx.range_pop()
     e.record()
     torch.cuda.synchronize()
     t = torch.tensor([s.elapsed_time(e) / steps], device=device)
@@ -449,6 +451,101 @@ def cpu_baseline_sample(reps=1):
     return {"value": round(attn_flops(c) / t / 1e12, 5), "unit": "TFLOP/s", "cores": int(cores),
             "kind": "port", "sample": "oracle fwd+bwd, encoder_self softplus B=1 H=12 L=1500 D=64 fp32 "
                                      f"({t:.2f} s per sample, best of {reps})"}
+
+
+def e2e_bench(torch, r, c, device, world, n_steps, chunks=None):
+    """The headline step end to end through STauOpusAttentionFunction with
+    pinned host buffers: every step copies Q, K, V, dO in and dQ, dK, dV,
+    dlog_tau, dlog_alpha out, timed with CUDA events over n_steps steps (max
+    over ranks). `chunks` lists the batch sizes the step is cut into."""
+    import torch.distributed as dist
+    from tau_dxb_b200.attention import STauOpusAttentionFunction
+    cs = torch.cuda.current_stream()
+    flops = attn_flops(c)
+    B, H, L, D = c["B"], c["H"], c["Lq"], c["D"]
+    hq = [r.Q.cpu().pin_memory(), r.K.cpu().pin_memory(), r.V.cpu().pin_memory(), r.dO.cpu().pin_memory()]
+    h_out = [torch.empty(B, H, L, D, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+    lt = torch.randn(H, device=device) * 0.5
+    la = torch.zeros(H, device=device)
+    h2d = sum(x.numel() * x.element_size() for x in hq)
+    d2h = sum(x.numel() * x.element_size() for x in h_out) + 2 * H * 4
+
+    # PCIe carries ~55 GB/s each way, so the 147 MB of inputs take longer than
+    # the kernels. Every host->device copy is queued first on its own stream,
+    # so the link never waits for the host (each chunk's Python-side operator
+    # calls take ~0.5 ms); chunk k's kernels start when its inputs land, and its
+    # device->host copy runs on a third stream. Small first and last chunks
+    # shorten the pipeline's fill (first inputs) and drain (last outputs).
+    # Every chunk is one STauOpusAttentionFunction.apply + backward;
+    # dlog_tau / dlog_alpha are summed over the chunks on the device and read
+    # back once per step.
+    if chunks is None:
+        chunks = [2, 3, 3, 3, 3, 2] if B == 16 else [B]
+    assert sum(chunks) == B
+    spans, o = [], 0
+    for n in chunks:
+        spans.append(slice(o, o + n))
+        o += n
+    s_in, s_c, s_out = (torch.cuda.Stream(device) for _ in range(3))
+
+    def e2e_step():
+        for st in (s_in, s_c, s_out):
+            st.wait_stream(cs)
+        ins = []
+        with torch.cuda.stream(s_in):
+            for sl in spans:
+                t = [x[sl].to(device, non_blocking=True) for x in hq]
+                ev = torch.cuda.Event()
+                ev.record(s_in)
+                ins.append((t, ev))
+        with torch.cuda.stream(s_c):
+            dlt = torch.zeros(H, device=device)
+            dla = torch.zeros(H, device=device)
+        keep = []
+        for sl, ((q, k, v, g), ev_in) in zip(spans, ins):
+            with torch.cuda.stream(s_c):
+                s_c.wait_event(ev_in)
+                q.requires_grad_(); k.requires_grad_(); v.requires_grad_()
+                ltp = lt.clone().requires_grad_()
+                lap = la.clone().requires_grad_()
+                out, _ = STauOpusAttentionFunction.apply(q, k, v, ltp, lap, c["sigma"], None, c["scale"])
+                out.backward(g)
+                dlt.add_(ltp.grad)
+                dla.add_(lap.grad)
+                ev_c = torch.cuda.Event()
+                ev_c.record(s_c)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_c)
+                for dst, src in zip(h_out, (q.grad, k.grad, v.grad)):
+                    dst[sl].copy_(src, non_blocking=True)
+            keep += [q, k, v, g, out, ltp, lap]
+        cs.wait_stream(s_out)
+        cs.wait_stream(s_c)
+        return dlt.cpu(), dla.cpu()
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    n_e2e = n_steps
+    s2 = torch.cuda.Event(enable_timing=True)
+    e2 = torch.cuda.Event(enable_timing=True)
+    s2.record(cs)
+    for _ in range(n_e2e):
+        e2e_step()
+    e2.record(cs)
+    torch.cuda.synchronize()
+    te = torch.tensor([s2.elapsed_time(e2) / n_e2e], device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    return {"value": round(world * flops / (float(te.item()) * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "ms_per_step": round(float(te.item()), 3), "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h),
+            "path": "STauOpusAttentionFunction.apply + backward, pinned host Q/K/V/dO in, "
+                    "dQ/dK/dV/dlog_tau/dlog_alpha out",
+            "pipeline": f"batch chunks {chunks}; all H2D queued first, kernels and D2H per chunk, "
+                        "three streams"}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -502,78 +599,7 @@ def run_ours(args, rank, world, local_rank):
     # ---- end-to-end through the public API with host buffers ----
     e2e = None
     if not args.no_e2e:
-        from tau_dxb_b200.attention import STauOpusAttentionFunction
-        B, H, L, D = c["B"], c["H"], c["Lq"], c["D"]
-        hq = [r.Q.cpu().pin_memory(), r.K.cpu().pin_memory(), r.V.cpu().pin_memory(), r.dO.cpu().pin_memory()]
-        h_out = [torch.empty(B, H, L, D, dtype=torch.bfloat16).pin_memory() for _ in range(3)]
-        lt = torch.randn(H, device=device) * 0.5
-        la = torch.zeros(H, device=device)
-        h2d = sum(x.numel() * x.element_size() for x in hq)
-        d2h = sum(x.numel() * x.element_size() for x in h_out) + 2 * H * 4
-
-        # The batch goes through in chunks on three streams, so the host->device
-        # copy of chunk k+1, the kernels of chunk k and the device->host copy
-        # of chunk k-1 overlap (PCIe is full duplex). Every chunk is one
-        # STauOpusAttentionFunction.apply + backward; dlog_tau / dlog_alpha
-        # are summed over the chunks on the device and read back once.
-        nch = next(n for n in (4, 2, 1) if B % n == 0)
-        cb = B // nch
-        s_in, s_c, s_out = (torch.cuda.Stream(device) for _ in range(3))
-
-        def e2e_step():
-            for st in (s_in, s_c, s_out):
-                st.wait_stream(cs)
-            keep = []
-            with torch.cuda.stream(s_c):
-                dlt = torch.zeros(H, device=device)
-                dla = torch.zeros(H, device=device)
-            for ch in range(nch):
-                sl = slice(ch * cb, (ch + 1) * cb)
-                with torch.cuda.stream(s_in):
-                    q, k, v, g = (x[sl].to(device, non_blocking=True) for x in hq)
-                    ev_in = torch.cuda.Event()
-                    ev_in.record(s_in)
-                with torch.cuda.stream(s_c):
-                    s_c.wait_event(ev_in)
-                    q.requires_grad_(); k.requires_grad_(); v.requires_grad_()
-                    ltp = lt.clone().requires_grad_()
-                    lap = la.clone().requires_grad_()
-                    out, _ = STauOpusAttentionFunction.apply(q, k, v, ltp, lap, c["sigma"], None, c["scale"])
-                    out.backward(g)
-                    dlt.add_(ltp.grad)
-                    dla.add_(lap.grad)
-                    ev_c = torch.cuda.Event()
-                    ev_c.record(s_c)
-                with torch.cuda.stream(s_out):
-                    s_out.wait_event(ev_c)
-                    for dst, src in zip(h_out, (q.grad, k.grad, v.grad)):
-                        dst[sl].copy_(src, non_blocking=True)
-                keep += [q, k, v, g, out, ltp, lap]
-            cs.wait_stream(s_out)
-            cs.wait_stream(s_c)
-            return dlt.cpu(), dla.cpu()
-
-        for _ in range(2):
-            e2e_step()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        n_e2e = max(3, args.steps // 4)
-        s2 = torch.cuda.Event(enable_timing=True)
-        e2 = torch.cuda.Event(enable_timing=True)
-        s2.record(cs)
-        for _ in range(n_e2e):
-            e2e_step()
-        e2.record(cs)
-        torch.cuda.synchronize()
-        te = torch.tensor([s2.elapsed_time(e2) / n_e2e], device=device)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": round(world * flops / (float(te.item()) * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-               "ms_per_step": round(float(te.item()), 3), "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h),
-               "path": "STauOpusAttentionFunction.apply + backward, pinned host Q/K/V/dO in, dQ/dK/dV/dlog_tau/dlog_alpha out",
-               "pipeline": f"{nch} batch chunks of {cb}; H2D, kernels and D2H on three streams"}
+        e2e = e2e_bench(torch, r, c, device, world, max(3, args.steps // 4))
     del r
     torch.cuda.empty_cache()
 
@@ -705,6 +731,8 @@ def main():
                     help="only the WTA sub-benchmark (JSON of its results; for ncu captures)")
     ap.add_argument("--tau-star-only", action="store_true",
                     help="only the tau* solver sub-benchmark (JSON of its results; for ncu captures)")
+    ap.add_argument("--train-only", action="store_true",
+                    help="only the Whisper train-step sub-benchmark (JSON of its results; for ncu launch lists)")
     args = ap.parse_args()
     if args.profile_batch:
         args.quick = args.no_e2e = args.no_cpu = args.no_train = True
@@ -728,6 +756,15 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+    if args.train_only:
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        ts = train_sub_bench(torch, device, world, rank, steps=args.steps, warmup=args.warmup)
+        if rank == 0:
+            _emit(json.dumps({"train_step": ts}), json_fd)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if args.wta_only or args.tau_star_only:
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)

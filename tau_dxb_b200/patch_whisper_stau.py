@@ -14,7 +14,15 @@ as in the reference), and transformers' module-global
 `eager_attention_forward` is swapped for one that runs the fused operator.
 `use_flash` is accepted for signature compatibility; there is one operator.
 
-One addition: `assume_causal_decoder=True` tells the decoder self-attention
+Each patched WhisperAttention also gets a forward that hands the operator
+the q/k/v projections as strided [B,H,L,D] views, with the 1/sqrt(d) scale
+passed to the kernel, instead of transformers' `.transpose(1, 2).contiguous()`
+copies and its separate `q * scaling` pass (three activation-sized copies and
+one multiply per call). The scale is 2^-3 for Whisper's head size, so scaling
+q in bf16 and scaling inside the kernel give the same bits. Calls with a KV
+cache (generation) go through transformers' own forward.
+
+`assume_causal_decoder=True` tells the decoder self-attention
 sites that their additive mask is the plain causal mask (true in training
 with labels and no decoder padding mask); the kernels then apply causality
 from indices instead of reading the [B,1,L,L] mask tensor. Results are the
@@ -25,6 +33,7 @@ from __future__ import annotations
 import json
 import math
 import re
+import types
 from pathlib import Path
 from typing import Dict, Union
 
@@ -126,6 +135,29 @@ def _make_learnable_stau_forward():
     return stau_eager_attention_forward
 
 
+def stau_whisper_attention_forward(self, hidden_states, key_value_states=None, past_key_values=None,
+                                   attention_mask=None, output_attentions=False, **kwargs):
+    """WhisperAttention.forward for a module with `_stau_opus`, without layout
+    copies: q, k and v stay [B,L,H,D] projections viewed as [B,H,L,D], the
+    operator writes its output as a [B,H,L,D] view of a [B,L,H,D] buffer, and
+    out_proj reads that buffer directly. Same values as transformers' forward
+    followed by the operator (its q * scaling with scaling = 2^-3 is exact in
+    bf16). With a KV cache it is transformers' forward unchanged."""
+    if past_key_values is not None:
+        return type(self).forward(self, hidden_states, key_value_states=key_value_states,
+                                  past_key_values=past_key_values, attention_mask=attention_mask,
+                                  output_attentions=output_attentions, **kwargs)
+    bsz, tgt_len = hidden_states.shape[:-1]
+    src = key_value_states if key_value_states is not None else hidden_states
+    q = self.q_proj(hidden_states).view(bsz, tgt_len, -1, self.head_dim).transpose(1, 2)
+    k = self.k_proj(src).view(bsz, -1, self.num_heads, self.head_dim).transpose(1, 2)
+    v = self.v_proj(src).view(bsz, -1, self.num_heads, self.head_dim).transpose(1, 2)
+    out = self._stau_opus(q, k, v, attn_mask=attention_mask, scale=self.scaling)
+    out = F.dropout(out, p=self.dropout if self.training else 0.0, training=self.training)
+    out = out.transpose(1, 2).reshape(bsz, tgt_len, -1)
+    return self.out_proj(out), None
+
+
 def _sigma_map(sigma_name):
     if isinstance(sigma_name, str):
         return {k: sigma_name for k in SITE_KINDS}
@@ -172,6 +204,7 @@ def apply_learnable_stau(model, tau_init=1.0, alpha_init: float = 1.0, sigma_nam
                                          dtype=opus.log_tau.dtype, device=opus.log_tau.device)
         opus.assume_causal = bool(assume_causal_decoder and kind == "decoder_self")
         module._stau_opus = opus
+        module.forward = types.MethodType(stau_whisper_attention_forward, module)
         n_attached += 1
     print(f"[tau-opus] Attached fused B200 STauOpus to {n_attached} attention modules")
     print(f"  sigma config: {sigma_map}")
@@ -188,3 +221,4 @@ def remove_stau(model=None):
                 module._stau_tau = None
                 if "_stau_opus" in module._modules:
                     del module._modules["_stau_opus"]
+                module.__dict__.pop("forward", None)

@@ -98,8 +98,25 @@ def build_model(cfg: StepConfig, device, tau_init=None):
     SG.apply_sparse_grad_wta(model, target="encoder+decoder", encoder_mode="wta_activation",
                              decoder_mode="sparse_grad", learnable_k=True,
                              init_k_ratio=cfg.init_k_ratio, track_wins=True)
+    model._tau_dxb_encoder_hook = contiguous_encoder_stream(model)
     model.train()
     return model
+
+
+def contiguous_encoder_stream(model):
+    """Make the encoder's residual stream row-major once, before its first layer.
+
+    Whisper's encoder forms it as conv2(x).permute(0, 2, 1) + positions, a
+    [B, L, d] tensor laid out as [B, d, L]; every residual add keeps that
+    layout, so each encoder layer norm copies its input to a contiguous buffer
+    in the forward and again in the backward, and the adds and the casts of
+    their gradients run as strided kernels. One copy here leaves the values
+    unchanged and the rest of the encoder row-major."""
+    def pre_hook(module, args):
+        if args and isinstance(args[0], torch.Tensor) and not args[0].is_contiguous():
+            return (args[0].contiguous(),) + tuple(args[1:])
+        return None
+    return model.model.encoder.layers[0].register_forward_pre_hook(pre_hook)
 
 
 def lr_lambda(warmup_steps: int, t0_steps: int, t_mult: int):

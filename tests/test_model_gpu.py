@@ -64,3 +64,38 @@ def test_bf16_autocast_train_step_runs_on_tensor_cores():
     assert C.lib().tau_dxb_device_error(1) == 0
     for n, p in step.model.named_parameters():
         assert torch.isfinite(p).all(), n
+
+
+def test_strided_attention_forward_matches_transformers_path():
+    """The patched WhisperAttention forward (q/k/v as strided views, the
+    1/sqrt(d) scale given to the kernel) and the row-major encoder stream give
+    the values of transformers' own forward (contiguous copies, q * scaling in
+    bf16) followed by the operator: the same loss, and gradients equal up to
+    the order of the backward's fp32 reductions."""
+    from tau_dxb_b200 import train as T
+    cfg = tiny_cfg(batch=2)
+    mel, labels = T.synthetic_batch(cfg, "cuda", torch.Generator().manual_seed(11))
+    model = T.build_model(cfg, "cuda")
+
+    def run():
+        model.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = model(input_features=mel, labels=labels)
+        out.loss.backward()
+        return float(out.loss), {n: p.grad.detach().float().cpu() for n, p in model.named_parameters()
+                                 if p.grad is not None}
+
+    loss_a, ga = run()
+    n_patched = 0
+    for m in model.modules():
+        if hasattr(m, "_stau_opus") and "forward" in m.__dict__:
+            del m.__dict__["forward"]
+            n_patched += 1
+    model._tau_dxb_encoder_hook.remove()
+    loss_b, gb = run()
+    assert n_patched == 3 * cfg.encoder_layers     # encoder self + decoder self + cross per layer pair
+    assert abs(loss_a - loss_b) <= 1e-6 * abs(loss_b), (loss_a, loss_b)
+    assert set(ga) == set(gb)
+    for n in ga:
+        assert rel_err(ga[n], gb[n]) < 1e-2, (n, rel_err(ga[n], gb[n]))
+
