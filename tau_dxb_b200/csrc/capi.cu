@@ -55,6 +55,11 @@ int whisper_log_mel_impl(const float*, int64_t, int64_t, const float*, float*, v
 int tau_star_solve_impl(const float*, int64_t, int64_t, int64_t, int32_t, int32_t, float, float, float, float,
                         float*, float*, cudaStream_t);
 int tau_star_analytic_impl(const float*, int64_t, int64_t, int64_t, int32_t, float*, cudaStream_t);
+size_t layer_norm_bwd_workspace(int64_t M, int64_t N);
+int layer_norm_fwd_impl(const float*, int64_t, int64_t, const float*, const float*, float, float*, float*, float*,
+                        cudaStream_t);
+int layer_norm_bwd_impl(const float*, const float*, const float*, const float*, const float*, int64_t, int64_t,
+                        float*, float*, float*, void*, size_t, cudaStream_t);
 
 namespace {
 
@@ -247,6 +252,22 @@ int tau_star_analytic(const float* scores, int64_t n_rows, int64_t T, int64_t ro
                       float* tau_out, void* stream) {
   g_last_error[0] = 0;
   return tau_star_analytic_impl(scores, n_rows, T, row_stride, sigma, tau_out, static_cast<cudaStream_t>(stream));
+}
+
+int tau_layer_norm_fwd(const float* x, int64_t M, int64_t d, const float* gamma, const float* beta, float eps,
+                       float* y, float* mean, float* rstd, void* stream) {
+  g_last_error[0] = 0;
+  return layer_norm_fwd_impl(x, M, d, gamma, beta, eps, y, mean, rstd, static_cast<cudaStream_t>(stream));
+}
+
+size_t tau_layer_norm_bwd_workspace_bytes(int64_t M, int64_t d) { return layer_norm_bwd_workspace(M, d); }
+
+int tau_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
+                       int64_t M, int64_t d, float* dx, float* dgamma, float* dbeta, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  g_last_error[0] = 0;
+  return layer_norm_bwd_impl(dy, x, mean, rstd, gamma, M, d, dx, dgamma, dbeta, workspace, workspace_bytes,
+                             static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

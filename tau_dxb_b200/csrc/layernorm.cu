@@ -1,0 +1,254 @@
+// fp32 LayerNorm forward and backward for the Whisper train step's 62 layer
+// norms (d = 768; rows = batch x frames), as autocast runs them: fp32 input,
+// weight and bias, fp32 output. Both kernels are HBM-bound row sweeps:
+//
+//   forward : one warp per row, the row in registers (d / 128 float4 chunks per
+//             lane); mean, then the variance about it (no E[x^2] - mean^2
+//             cancellation), y = (x - mean) rstd gamma + beta; writes y, mean,
+//             rstd. 8 bytes per element.
+//   backward: one warp per row, persistent CTAs; per row xhat = (x - mean) rstd,
+//             g = gamma dy, dx = rstd (g - mean(g) - xhat mean(g xhat)), and
+//             per-column dgamma += dy xhat, dbeta += dy kept in registers over
+//             all of a warp's rows; the warps of a CTA add theirs in shared
+//             memory into one partial row per CTA, and a second kernel sums the
+//             partial rows column by column in a fixed order (deterministic).
+//             12 bytes per element plus 2 x 4 x d per CTA.
+
+#include "common.cuh"
+
+namespace taudxb {
+namespace {
+
+constexpr int kLnWarps = 8;            // rows in flight per CTA
+constexpr uint32_t kFull = 0xffffffffu;
+
+__device__ __forceinline__ float ln_warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(kLnWarps * 32)
+ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
+              float eps, int64_t M, float* __restrict__ y, float* __restrict__ mean_out,
+              float* __restrict__ rstd_out) {
+  constexpr int N = NCH * 128;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kLnWarps;
+  float4 g[NCH], b[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    g[c] = __ldg(reinterpret_cast<const float4*>(gamma) + c * 32 + lane);
+    b[c] = __ldg(reinterpret_cast<const float4*>(beta) + c * 32 + lane);
+  }
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarps + (threadIdx.x >> 5); row < M; row += warps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * N);
+    float4 v[NCH];
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      v[c] = __ldcs(xr + c * 32 + lane);
+      s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
+    }
+    const float mean = ln_warp_sum(s) * (1.f / N);
+    float q = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const float a = v[c].x - mean, bb = v[c].y - mean, cc = v[c].z - mean, d = v[c].w - mean;
+      q = fmaf(a, a, fmaf(bb, bb, fmaf(cc, cc, fmaf(d, d, q))));
+    }
+    const float rstd = rsqrtf(ln_warp_sum(q) * (1.f / N) + eps);
+    float4* yr = reinterpret_cast<float4*>(y + row * N);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      float4 o;
+      o.x = fmaf((v[c].x - mean) * rstd, g[c].x, b[c].x);
+      o.y = fmaf((v[c].y - mean) * rstd, g[c].y, b[c].y);
+      o.z = fmaf((v[c].z - mean) * rstd, g[c].z, b[c].z);
+      o.w = fmaf((v[c].w - mean) * rstd, g[c].w, b[c].w);
+      yr[c * 32 + lane] = o;
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(kLnWarps * 32)
+ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean_in,
+              const float* __restrict__ rstd_in, const float* __restrict__ gamma, int64_t M,
+              float* __restrict__ dx, float* __restrict__ part_dg, float* __restrict__ part_db) {
+  constexpr int N = NCH * 128;
+  __shared__ float4 red[kLnWarps][NCH * 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kLnWarps;
+  float4 g[NCH], adg[NCH], adb[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    g[c] = __ldg(reinterpret_cast<const float4*>(gamma) + c * 32 + lane);
+    adg[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    adb[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarps + warp; row < M; row += warps) {
+    const float4* dyr = reinterpret_cast<const float4*>(dy + row * N);
+    const float4* xr = reinterpret_cast<const float4*>(x + row * N);
+    const float mean = __ldg(mean_in + row), rstd = __ldg(rstd_in + row);
+    float4 d[NCH], xh[NCH];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      d[c] = __ldcs(dyr + c * 32 + lane);
+      const float4 xv = __ldcs(xr + c * 32 + lane);
+      xh[c] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd, (xv.w - mean) * rstd);
+      const float gx = g[c].x * d[c].x, gy = g[c].y * d[c].y, gz = g[c].z * d[c].z, gw = g[c].w * d[c].w;
+      s1 += (gx + gy) + (gz + gw);
+      s2 = fmaf(gx, xh[c].x, fmaf(gy, xh[c].y, fmaf(gz, xh[c].z, fmaf(gw, xh[c].w, s2))));
+      adg[c].x = fmaf(d[c].x, xh[c].x, adg[c].x);
+      adg[c].y = fmaf(d[c].y, xh[c].y, adg[c].y);
+      adg[c].z = fmaf(d[c].z, xh[c].z, adg[c].z);
+      adg[c].w = fmaf(d[c].w, xh[c].w, adg[c].w);
+      adb[c].x += d[c].x;
+      adb[c].y += d[c].y;
+      adb[c].z += d[c].z;
+      adb[c].w += d[c].w;
+    }
+    const float m1 = ln_warp_sum(s1) * (1.f / N), m2 = ln_warp_sum(s2) * (1.f / N);
+    float4* dxr = reinterpret_cast<float4*>(dx + row * N);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      float4 o;
+      o.x = rstd * (g[c].x * d[c].x - m1 - xh[c].x * m2);
+      o.y = rstd * (g[c].y * d[c].y - m1 - xh[c].y * m2);
+      o.z = rstd * (g[c].z * d[c].z - m1 - xh[c].z * m2);
+      o.w = rstd * (g[c].w * d[c].w - m1 - xh[c].w * m2);
+      dxr[c * 32 + lane] = o;
+    }
+  }
+  // this CTA's column partials: warps in a fixed order through shared memory,
+  // dgamma then dbeta through the same buffer
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) red[warp][c * 32 + lane] = which ? adb[c] : adg[c];
+    __syncthreads();
+    for (int col4 = threadIdx.x; col4 < NCH * 32; col4 += kLnWarps * 32) {
+      float4 acc = red[0][col4];
+#pragma unroll
+      for (int w = 1; w < kLnWarps; ++w) {
+        const float4 v = red[w][col4];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      float* dst = (which ? part_db : part_dg) + static_cast<int64_t>(blockIdx.x) * N;
+      reinterpret_cast<float4*>(dst)[col4] = acc;
+    }
+    __syncthreads();
+  }
+}
+
+// dgamma[c] = sum_b part_dg[b][c], dbeta likewise; one thread per column.
+__global__ void ln_bwd_reduce_kernel(const float* __restrict__ part_dg, const float* __restrict__ part_db,
+                                     int parts, int N, float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= 2 * N) return;
+  const float* src = col < N ? part_dg + col : part_db + (col - N);
+  float acc = 0.f;
+  for (int b = 0; b < parts; ++b) acc += src[static_cast<int64_t>(b) * N];
+  if (col < N) dgamma[col] = acc;
+  else dbeta[col - N] = acc;
+}
+
+int ln_parts(int64_t M) {
+  const int64_t want = (M + kLnWarps - 1) / kLnWarps;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 2;
+  return static_cast<int>(want < cap ? (want < 1 ? 1 : want) : cap);
+}
+
+template <template <int> class Launch, typename... A>
+int dispatch_nch(int N, A... args) {
+  switch (N / 128) {
+    case 1: return Launch<1>::run(args...);
+    case 2: return Launch<2>::run(args...);
+    case 3: return Launch<3>::run(args...);
+    case 4: return Launch<4>::run(args...);
+    case 5: return Launch<5>::run(args...);
+    case 6: return Launch<6>::run(args...);
+    case 7: return Launch<7>::run(args...);
+    case 8: return Launch<8>::run(args...);
+    default: return fail(TAU_DXB_ERR_UNSUPPORTED, "layer norm: d = %d unsupported", N);
+  }
+}
+
+template <int NCH>
+struct FwdLaunch {
+  static int run(const float* x, const float* g, const float* b, float eps, int64_t M, float* y, float* mean,
+                 float* rstd, cudaStream_t st) {
+    const int grid = static_cast<int>((M + kLnWarps - 1) / kLnWarps < 8ll * sm_count()
+                                          ? (M + kLnWarps - 1) / kLnWarps : 8ll * sm_count());
+    ln_fwd_kernel<NCH><<<grid, kLnWarps * 32, 0, st>>>(x, g, b, eps, M, y, mean, rstd);
+    return check_launch("ln_fwd_kernel");
+  }
+};
+
+template <int NCH>
+struct BwdLaunch {
+  static int run(const float* dy, const float* x, const float* mean, const float* rstd, const float* g, int64_t M,
+                 float* dx, float* pdg, float* pdb, int parts, cudaStream_t st) {
+    ln_bwd_kernel<NCH><<<parts, kLnWarps * 32, 0, st>>>(dy, x, mean, rstd, g, M, dx, pdg, pdb);
+    return check_launch("ln_bwd_kernel");
+  }
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+size_t layer_norm_bwd_workspace(int64_t M, int64_t N) {
+  if (M <= 0 || N <= 0) return 0;
+  return static_cast<size_t>(ln_parts(M)) * static_cast<size_t>(N) * 2 * sizeof(float);
+}
+
+int layer_norm_fwd_impl(const float* x, int64_t M, int64_t N, const float* gamma, const float* beta, float eps,
+                        float* y, float* mean, float* rstd, cudaStream_t st) {
+  TDX_CHECK_ARG(M >= 0 && N > 0 && N % 128 == 0 && N <= 1024,
+                "layer norm: need d a multiple of 128 up to 1024 (got %lld)", (long long)N);
+  if (M == 0) return TAU_DXB_OK;
+  TDX_CHECK_ARG(x && gamma && beta && y && mean && rstd, "layer norm: null pointer");
+  TDX_CHECK_ARG(aligned16(x) && aligned16(gamma) && aligned16(beta) && aligned16(y),
+                "layer norm: x, gamma, beta and y must be 16-byte aligned");
+  return dispatch_nch<FwdLaunch>(static_cast<int>(N), x, gamma, beta, eps, M, y, mean, rstd, st);
+}
+
+int layer_norm_bwd_impl(const float* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
+                        int64_t M, int64_t N, float* dx, float* dgamma, float* dbeta, void* workspace,
+                        size_t workspace_bytes, cudaStream_t st) {
+  TDX_CHECK_ARG(M >= 0 && N > 0 && N % 128 == 0 && N <= 1024,
+                "layer norm: need d a multiple of 128 up to 1024 (got %lld)", (long long)N);
+  TDX_CHECK_ARG(dgamma && dbeta, "layer norm: null pointer");
+  if (M == 0) {
+    TDX_CUDA(cudaMemsetAsync(dgamma, 0, N * sizeof(float), st));
+    TDX_CUDA(cudaMemsetAsync(dbeta, 0, N * sizeof(float), st));
+    return TAU_DXB_OK;
+  }
+  TDX_CHECK_ARG(dy && x && mean && rstd && gamma && dx && workspace, "layer norm: null pointer");
+  TDX_CHECK_ARG(aligned16(dy) && aligned16(x) && aligned16(gamma) && aligned16(dx) && aligned16(workspace),
+                "layer norm: dy, x, gamma, dx and the workspace must be 16-byte aligned");
+  const size_t need = layer_norm_bwd_workspace(M, N);
+  if (workspace_bytes < need)
+    return fail(TAU_DXB_ERR_WORKSPACE, "layer norm: workspace of %zu bytes, need %zu", workspace_bytes, need);
+  const int parts = ln_parts(M);
+  float* pdg = static_cast<float*>(workspace);
+  float* pdb = pdg + static_cast<size_t>(parts) * N;
+  int rc = dispatch_nch<BwdLaunch>(static_cast<int>(N), dy, x, mean, rstd, gamma, M, dx, pdg, pdb, parts, st);
+  if (rc) return rc;
+  const int threads = 256, blocks = static_cast<int>((2 * N + threads - 1) / threads);
+  ln_bwd_reduce_kernel<<<blocks, threads, 0, st>>>(pdg, pdb, parts, static_cast<int>(N), dgamma, dbeta);
+  return check_launch("ln_bwd_reduce_kernel");
+}
+
+}  // namespace taudxb

@@ -26,6 +26,7 @@ from dataclasses import dataclass, field
 import torch
 import torch.distributed as dist
 
+from . import layernorm as LN
 from . import patch_whisper_sparse_grad as SG
 from . import patch_whisper_stau as ST
 
@@ -99,6 +100,7 @@ def build_model(cfg: StepConfig, device, tau_init=None):
                              decoder_mode="sparse_grad", learnable_k=True,
                              init_k_ratio=cfg.init_k_ratio, track_wins=True)
     model._tau_dxb_encoder_hook = contiguous_encoder_stream(model)
+    LN.patch_layer_norms(model)
     model.train()
     return model
 
