@@ -22,6 +22,12 @@ one multiply per call). The scale is 2^-3 for Whisper's head size, so scaling
 q in bf16 and scaling inside the kernel give the same bits. Calls with a KV
 cache (generation) go through transformers' own forward.
 
+`fuse_qkv=True` computes q, k and v with one GEMM over the concatenated
+projection weights (k and v for cross-attention): the shared input is cast to
+bf16 once and its gradient is one tensor, instead of three casts, three casts
+back and two adds. Parameters stay separate; values change at the level of
+rounding (one fp32 accumulation over 3 x d instead of three).
+
 `assume_causal_decoder=True` tells the decoder self-attention
 sites that their additive mask is the plain causal mask (true in training
 with labels and no decoder padding mask); the kernels then apply causality
@@ -149,13 +155,41 @@ def stau_whisper_attention_forward(self, hidden_states, key_value_states=None, p
                                   output_attentions=output_attentions, **kwargs)
     bsz, tgt_len = hidden_states.shape[:-1]
     src = key_value_states if key_value_states is not None else hidden_states
-    q = self.q_proj(hidden_states).view(bsz, tgt_len, -1, self.head_dim).transpose(1, 2)
-    k = self.k_proj(src).view(bsz, -1, self.num_heads, self.head_dim).transpose(1, 2)
-    v = self.v_proj(src).view(bsz, -1, self.num_heads, self.head_dim).transpose(1, 2)
+    if getattr(self, "_stau_fused_qkv", False):
+        q, k, v = _fused_projections(self, hidden_states, key_value_states)
+    else:
+        q = self.q_proj(hidden_states)
+        k = self.k_proj(src)
+        v = self.v_proj(src)
+    q = q.view(bsz, tgt_len, -1, self.head_dim).transpose(1, 2)
+    k = k.view(bsz, -1, self.num_heads, self.head_dim).transpose(1, 2)
+    v = v.view(bsz, -1, self.num_heads, self.head_dim).transpose(1, 2)
     out = self._stau_opus(q, k, v, attn_mask=attention_mask, scale=self.scaling)
     out = F.dropout(out, p=self.dropout if self.training else 0.0, training=self.training)
     out = out.transpose(1, 2).reshape(bsz, tgt_len, -1)
     return self.out_proj(out), None
+
+
+def _proj_bias(lin, like):
+    return lin.bias if lin.bias is not None else torch.zeros(lin.out_features, dtype=like.dtype, device=like.device)
+
+
+def _fused_projections(self, hidden_states, key_value_states):
+    """q, k, v from one GEMM over the concatenated weights (k and v only for
+    cross-attention, whose q reads the decoder stream): the shared input is
+    cast to bf16 once under autocast, and its gradient comes back as one
+    tensor instead of three cast back to fp32 and added. Parameters stay
+    separate (same state_dict); the outputs are strided views of one buffer."""
+    wq, wk, wv = self.q_proj.weight, self.k_proj.weight, self.v_proj.weight
+    if key_value_states is None:
+        w = torch.cat([wq, wk, wv], 0)
+        b = torch.cat([_proj_bias(self.q_proj, wq), _proj_bias(self.k_proj, wq), _proj_bias(self.v_proj, wq)])
+        return F.linear(hidden_states, w, b).split([wq.shape[0], wk.shape[0], wv.shape[0]], dim=-1)
+    q = self.q_proj(hidden_states)
+    w = torch.cat([wk, wv], 0)
+    b = torch.cat([_proj_bias(self.k_proj, wk), _proj_bias(self.v_proj, wk)])
+    k, v = F.linear(key_value_states, w, b).split([wk.shape[0], wv.shape[0]], dim=-1)
+    return q, k, v
 
 
 def _sigma_map(sigma_name):
@@ -168,7 +202,7 @@ def _sigma_map(sigma_name):
 
 def apply_learnable_stau(model, tau_init=1.0, alpha_init: float = 1.0, sigma_name="softplus",
                          default_tau_json=None, use_flash: bool = False,
-                         assume_causal_decoder: bool = False):
+                         assume_causal_decoder: bool = False, fuse_qkv: bool = False):
     """Attach a learnable tau-opus operator to every WhisperAttention module."""
     if isinstance(tau_init, (str, Path)):
         if str(tau_init).lower() == "tau_star":
@@ -204,6 +238,7 @@ def apply_learnable_stau(model, tau_init=1.0, alpha_init: float = 1.0, sigma_nam
                                          dtype=opus.log_tau.dtype, device=opus.log_tau.device)
         opus.assume_causal = bool(assume_causal_decoder and kind == "decoder_self")
         module._stau_opus = opus
+        module._stau_fused_qkv = bool(fuse_qkv)
         module.forward = types.MethodType(stau_whisper_attention_forward, module)
         n_attached += 1
     print(f"[tau-opus] Attached fused B200 STauOpus to {n_attached} attention modules")

@@ -95,7 +95,7 @@ def build_model(cfg: StepConfig, device, tau_init=None):
     torch.manual_seed(cfg.seed)
     model = WhisperForConditionalGeneration(whisper_config(cfg)).to(device)
     ST.apply_learnable_stau(model, tau_init=tau_init if tau_init is not None else synthetic_tau_init(cfg),
-                            alpha_init=1.0, sigma_name=SIGMA_MAP, assume_causal_decoder=True)
+                            alpha_init=1.0, sigma_name=SIGMA_MAP, assume_causal_decoder=True, fuse_qkv=True)
     SG.apply_sparse_grad_wta(model, target="encoder+decoder", encoder_mode="wta_activation",
                              decoder_mode="sparse_grad", learnable_k=True,
                              init_k_ratio=cfg.init_k_ratio, track_wins=True)

@@ -85,6 +85,9 @@ def test_strided_attention_forward_matches_transformers_path():
         return float(out.loss), {n: p.grad.detach().float().cpu() for n, p in model.named_parameters()
                                  if p.grad is not None}
 
+    for m in model.modules():                      # the layout change alone: exact
+        if hasattr(m, "_stau_fused_qkv"):
+            m._stau_fused_qkv = False
     loss_a, ga = run()
     n_patched = 0
     for m in model.modules():
@@ -98,4 +101,32 @@ def test_strided_attention_forward_matches_transformers_path():
     assert set(ga) == set(gb)
     for n in ga:
         assert rel_err(ga[n], gb[n]) < 1e-2, (n, rel_err(ga[n], gb[n]))
+
+
+def test_fused_qkv_projection_matches_separate_projections():
+    """fuse_qkv (one GEMM over [Wq; Wk; Wv], [Wk; Wv] for cross-attention)
+    against the three projections: bf16 autocast step, same loss and
+    gradients up to bf16 rounding."""
+    from tau_dxb_b200 import train as T
+    cfg = tiny_cfg(batch=2)
+    mel, labels = T.synthetic_batch(cfg, "cuda", torch.Generator().manual_seed(12))
+    model = T.build_model(cfg, "cuda")
+
+    def run(fused):
+        for m in model.modules():
+            if hasattr(m, "_stau_fused_qkv"):
+                m._stau_fused_qkv = fused
+        model.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = model(input_features=mel, labels=labels)
+        out.loss.backward()
+        return float(out.loss), {n: p.grad.detach().float().cpu() for n, p in model.named_parameters()
+                                 if p.grad is not None}
+
+    loss_f, gf = run(True)
+    loss_s, gs = run(False)
+    assert abs(loss_f - loss_s) <= 2e-3 * abs(loss_s), (loss_f, loss_s)
+    assert set(gf) == set(gs)
+    for n in gf:
+        assert rel_err(gf[n], gs[n]) < 3e-2, (n, rel_err(gf[n], gs[n]))
 
