@@ -276,24 +276,27 @@ TAU_DXB_API int tau_star_analytic(const float* scores, int64_t n_rows, int64_t T
  * (transformers' WhisperEncoderLayer / WhisperDecoderLayer norms and the two
  * final norms): y = (x - mean) * rstd * gamma + beta with
  * rstd = 1 / sqrt(var + eps), var the biased variance.
- * x, y: fp32 [M, d] contiguous; gamma, beta: fp32 [d]; mean, rstd: fp32 [M]
- * (saved for the backward). d a multiple of 128 up to 1024; x, y, gamma and
- * beta 16-byte aligned.
+ * x: fp32 [M, d] contiguous; y: [M, d] of y_dtype (TAU_DXB_F32, or TAU_DXB_BF16
+ * rounded to nearest even -- what autocast would cast the fp32 output to for a
+ * bf16 GEMM that is its only consumer); gamma, beta: fp32 [d]; mean, rstd:
+ * fp32 [M] (saved for the backward). d a multiple of 128 up to 1024; x, y,
+ * gamma and beta 16-byte aligned.
  */
 TAU_DXB_API int tau_layer_norm_fwd(const float* x, int64_t M, int64_t d, const float* gamma,
-                                   const float* beta, float eps, float* y, float* mean, float* rstd,
-                                   void* stream);
+                                   const float* beta, float eps, void* y, int32_t y_dtype,
+                                   float* mean, float* rstd, void* stream);
 
 /*
- * Its backward: dx [M, d], and dgamma, dbeta [d] summed over the rows in a
- * fixed order (the same bits on every call). workspace: device memory of
+ * Its backward: dy [M, d] of dy_dtype (fp32 or bf16), dx fp32 [M, d], and
+ * dgamma, dbeta [d] summed over the rows in a fixed order (the same bits on
+ * every call). workspace: device memory of
  * tau_layer_norm_bwd_workspace_bytes(M, d) bytes, 16-byte aligned.
  */
 TAU_DXB_API size_t tau_layer_norm_bwd_workspace_bytes(int64_t M, int64_t d);
-TAU_DXB_API int tau_layer_norm_bwd(const float* dy, const float* x, const float* mean,
-                                   const float* rstd, const float* gamma, int64_t M, int64_t d,
-                                   float* dx, float* dgamma, float* dbeta, void* workspace,
-                                   size_t workspace_bytes, void* stream);
+TAU_DXB_API int tau_layer_norm_bwd(const void* dy, int32_t dy_dtype, const float* x,
+                                   const float* mean, const float* rstd, const float* gamma,
+                                   int64_t M, int64_t d, float* dx, float* dgamma, float* dbeta,
+                                   void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -75,9 +75,9 @@ SIGNATURES = {
     "tau_star_solve": (ctypes.c_int, [_vp, _i64, _i64, _i64, _i32, _i32, ctypes.c_float, ctypes.c_float,
                                       ctypes.c_float, ctypes.c_float, _vp, _vp, _vp]),
     "tau_star_analytic": (ctypes.c_int, [_vp, _i64, _i64, _i64, _i32, _vp, _vp]),
-    "tau_layer_norm_fwd": (ctypes.c_int, [_vp, _i64, _i64, _vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp]),
+    "tau_layer_norm_fwd": (ctypes.c_int, [_vp, _i64, _i64, _vp, _vp, ctypes.c_float, _vp, _i32, _vp, _vp, _vp]),
     "tau_layer_norm_bwd_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
-    "tau_layer_norm_bwd": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
+    "tau_layer_norm_bwd": (ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
                                           ctypes.c_size_t, _vp]),
 }
 

@@ -56,10 +56,10 @@ int tau_star_solve_impl(const float*, int64_t, int64_t, int64_t, int32_t, int32_
                         float*, float*, cudaStream_t);
 int tau_star_analytic_impl(const float*, int64_t, int64_t, int64_t, int32_t, float*, cudaStream_t);
 size_t layer_norm_bwd_workspace(int64_t M, int64_t N);
-int layer_norm_fwd_impl(const float*, int64_t, int64_t, const float*, const float*, float, float*, float*, float*,
-                        cudaStream_t);
-int layer_norm_bwd_impl(const float*, const float*, const float*, const float*, const float*, int64_t, int64_t,
-                        float*, float*, float*, void*, size_t, cudaStream_t);
+int layer_norm_fwd_impl(const float*, int64_t, int64_t, const float*, const float*, float, void*, int32_t, float*,
+                        float*, cudaStream_t);
+int layer_norm_bwd_impl(const void*, int32_t, const float*, const float*, const float*, const float*, int64_t,
+                        int64_t, float*, float*, float*, void*, size_t, cudaStream_t);
 
 namespace {
 
@@ -255,19 +255,19 @@ int tau_star_analytic(const float* scores, int64_t n_rows, int64_t T, int64_t ro
 }
 
 int tau_layer_norm_fwd(const float* x, int64_t M, int64_t d, const float* gamma, const float* beta, float eps,
-                       float* y, float* mean, float* rstd, void* stream) {
+                       void* y, int32_t y_dtype, float* mean, float* rstd, void* stream) {
   g_last_error[0] = 0;
-  return layer_norm_fwd_impl(x, M, d, gamma, beta, eps, y, mean, rstd, static_cast<cudaStream_t>(stream));
+  return layer_norm_fwd_impl(x, M, d, gamma, beta, eps, y, y_dtype, mean, rstd, static_cast<cudaStream_t>(stream));
 }
 
 size_t tau_layer_norm_bwd_workspace_bytes(int64_t M, int64_t d) { return layer_norm_bwd_workspace(M, d); }
 
-int tau_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
-                       int64_t M, int64_t d, float* dx, float* dgamma, float* dbeta, void* workspace,
-                       size_t workspace_bytes, void* stream) {
+int tau_layer_norm_bwd(const void* dy, int32_t dy_dtype, const float* x, const float* mean, const float* rstd,
+                       const float* gamma, int64_t M, int64_t d, float* dx, float* dgamma, float* dbeta,
+                       void* workspace, size_t workspace_bytes, void* stream) {
   g_last_error[0] = 0;
-  return layer_norm_bwd_impl(dy, x, mean, rstd, gamma, M, d, dx, dgamma, dbeta, workspace, workspace_bytes,
-                             static_cast<cudaStream_t>(stream));
+  return layer_norm_bwd_impl(dy, dy_dtype, x, mean, rstd, gamma, M, d, dx, dgamma, dbeta, workspace,
+                             workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -4,15 +4,17 @@
 //
 //   forward : one warp per row, the row in registers (d / 128 float4 chunks per
 //             lane); mean, then the variance about it (no E[x^2] - mean^2
-//             cancellation), y = (x - mean) rstd gamma + beta; writes y, mean,
-//             rstd. 8 bytes per element.
+//             cancellation), y = (x - mean) rstd gamma + beta; writes y (fp32,
+//             or bf16 rounded to nearest even for a norm whose one consumer is
+//             a bf16 GEMM under autocast), mean, rstd. 8 (6) bytes per element.
 //   backward: one warp per row, persistent CTAs; per row xhat = (x - mean) rstd,
 //             g = gamma dy, dx = rstd (g - mean(g) - xhat mean(g xhat)), and
 //             per-column dgamma += dy xhat, dbeta += dy kept in registers over
 //             all of a warp's rows; the warps of a CTA add theirs in shared
 //             memory into one partial row per CTA, and a second kernel sums the
 //             partial rows column by column in a fixed order (deterministic).
-//             12 bytes per element plus 2 x 4 x d per CTA.
+//             dy is fp32 or bf16 (the gradient of a bf16 y). 12 (10) bytes per
+//             element plus 2 x 4 x d per CTA.
 
 #include "common.cuh"
 
@@ -28,10 +30,28 @@ __device__ __forceinline__ float ln_warp_sum(float v) {
   return v;
 }
 
-template <int NCH>
+// four fp32 values to memory as fp32 (16 B) or bf16 (8 B, round to nearest even)
+__device__ __forceinline__ void store4(float* p, int64_t i4, float4 v) { reinterpret_cast<float4*>(p)[i4] = v; }
+__device__ __forceinline__ void store4(__nv_bfloat16* p, int64_t i4, float4 v) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&lo);
+  u.y = *reinterpret_cast<const uint32_t*>(&hi);
+  reinterpret_cast<uint2*>(p)[i4] = u;
+}
+__device__ __forceinline__ float4 load4(const float* p, int64_t i4) {
+  return __ldcs(reinterpret_cast<const float4*>(p) + i4);
+}
+__device__ __forceinline__ float4 load4(const __nv_bfloat16* p, int64_t i4) {
+  const uint2 u = __ldcs(reinterpret_cast<const uint2*>(p) + i4);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
+template <int NCH, typename TY>
 __global__ void __launch_bounds__(kLnWarps * 32)
 ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
-              float eps, int64_t M, float* __restrict__ y, float* __restrict__ mean_out,
+              float eps, int64_t M, TY* __restrict__ y, float* __restrict__ mean_out,
               float* __restrict__ rstd_out) {
   constexpr int N = NCH * 128;
   const int lane = threadIdx.x & 31;
@@ -59,7 +79,7 @@ ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma, cons
       q = fmaf(a, a, fmaf(bb, bb, fmaf(cc, cc, fmaf(d, d, q))));
     }
     const float rstd = rsqrtf(ln_warp_sum(q) * (1.f / N) + eps);
-    float4* yr = reinterpret_cast<float4*>(y + row * N);
+    TY* yr = y + row * N;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       float4 o;
@@ -67,7 +87,7 @@ ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma, cons
       o.y = fmaf((v[c].y - mean) * rstd, g[c].y, b[c].y);
       o.z = fmaf((v[c].z - mean) * rstd, g[c].z, b[c].z);
       o.w = fmaf((v[c].w - mean) * rstd, g[c].w, b[c].w);
-      yr[c * 32 + lane] = o;
+      store4(yr, c * 32 + lane, o);
     }
     if (lane == 0) {
       mean_out[row] = mean;
@@ -76,9 +96,9 @@ ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma, cons
   }
 }
 
-template <int NCH>
+template <int NCH, typename TD>
 __global__ void __launch_bounds__(kLnWarps * 32)
-ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean_in,
+ln_bwd_kernel(const TD* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean_in,
               const float* __restrict__ rstd_in, const float* __restrict__ gamma, int64_t M,
               float* __restrict__ dx, float* __restrict__ part_dg, float* __restrict__ part_db) {
   constexpr int N = NCH * 128;
@@ -93,14 +113,14 @@ ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x, const f
     adb[c] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarps + warp; row < M; row += warps) {
-    const float4* dyr = reinterpret_cast<const float4*>(dy + row * N);
+    const TD* dyr = dy + row * N;
     const float4* xr = reinterpret_cast<const float4*>(x + row * N);
     const float mean = __ldg(mean_in + row), rstd = __ldg(rstd_in + row);
     float4 d[NCH], xh[NCH];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-      d[c] = __ldcs(dyr + c * 32 + lane);
+      d[c] = load4(dyr, c * 32 + lane);
       const float4 xv = __ldcs(xr + c * 32 + lane);
       xh[c] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd, (xv.w - mean) * rstd);
       const float gx = g[c].x * d[c].x, gy = g[c].y * d[c].y, gz = g[c].z * d[c].z, gw = g[c].w * d[c].w;
@@ -186,20 +206,29 @@ int dispatch_nch(int N, A... args) {
 
 template <int NCH>
 struct FwdLaunch {
-  static int run(const float* x, const float* g, const float* b, float eps, int64_t M, float* y, float* mean,
-                 float* rstd, cudaStream_t st) {
+  static int run(const float* x, const float* g, const float* b, float eps, int64_t M, void* y, int y_bf16,
+                 float* mean, float* rstd, cudaStream_t st) {
     const int grid = static_cast<int>((M + kLnWarps - 1) / kLnWarps < 8ll * sm_count()
                                           ? (M + kLnWarps - 1) / kLnWarps : 8ll * sm_count());
-    ln_fwd_kernel<NCH><<<grid, kLnWarps * 32, 0, st>>>(x, g, b, eps, M, y, mean, rstd);
+    if (y_bf16)
+      ln_fwd_kernel<NCH, __nv_bfloat16><<<grid, kLnWarps * 32, 0, st>>>(
+          x, g, b, eps, M, static_cast<__nv_bfloat16*>(y), mean, rstd);
+    else
+      ln_fwd_kernel<NCH, float><<<grid, kLnWarps * 32, 0, st>>>(x, g, b, eps, M, static_cast<float*>(y), mean, rstd);
     return check_launch("ln_fwd_kernel");
   }
 };
 
 template <int NCH>
 struct BwdLaunch {
-  static int run(const float* dy, const float* x, const float* mean, const float* rstd, const float* g, int64_t M,
-                 float* dx, float* pdg, float* pdb, int parts, cudaStream_t st) {
-    ln_bwd_kernel<NCH><<<parts, kLnWarps * 32, 0, st>>>(dy, x, mean, rstd, g, M, dx, pdg, pdb);
+  static int run(const void* dy, int dy_bf16, const float* x, const float* mean, const float* rstd, const float* g,
+                 int64_t M, float* dx, float* pdg, float* pdb, int parts, cudaStream_t st) {
+    if (dy_bf16)
+      ln_bwd_kernel<NCH, __nv_bfloat16><<<parts, kLnWarps * 32, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(dy), x, mean, rstd, g, M, dx, pdg, pdb);
+    else
+      ln_bwd_kernel<NCH, float><<<parts, kLnWarps * 32, 0, st>>>(static_cast<const float*>(dy), x, mean, rstd, g,
+                                                                 M, dx, pdg, pdb);
     return check_launch("ln_bwd_kernel");
   }
 };
@@ -214,19 +243,22 @@ size_t layer_norm_bwd_workspace(int64_t M, int64_t N) {
 }
 
 int layer_norm_fwd_impl(const float* x, int64_t M, int64_t N, const float* gamma, const float* beta, float eps,
-                        float* y, float* mean, float* rstd, cudaStream_t st) {
+                        void* y, int32_t y_dtype, float* mean, float* rstd, cudaStream_t st) {
+  TDX_CHECK_ARG(y_dtype == TAU_DXB_F32 || y_dtype == TAU_DXB_BF16, "layer norm: y must be fp32 or bf16");
   TDX_CHECK_ARG(M >= 0 && N > 0 && N % 128 == 0 && N <= 1024,
                 "layer norm: need d a multiple of 128 up to 1024 (got %lld)", (long long)N);
   if (M == 0) return TAU_DXB_OK;
   TDX_CHECK_ARG(x && gamma && beta && y && mean && rstd, "layer norm: null pointer");
   TDX_CHECK_ARG(aligned16(x) && aligned16(gamma) && aligned16(beta) && aligned16(y),
                 "layer norm: x, gamma, beta and y must be 16-byte aligned");
-  return dispatch_nch<FwdLaunch>(static_cast<int>(N), x, gamma, beta, eps, M, y, mean, rstd, st);
+  return dispatch_nch<FwdLaunch>(static_cast<int>(N), x, gamma, beta, eps, M, y,
+                                 static_cast<int>(y_dtype == TAU_DXB_BF16), mean, rstd, st);
 }
 
-int layer_norm_bwd_impl(const float* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
-                        int64_t M, int64_t N, float* dx, float* dgamma, float* dbeta, void* workspace,
-                        size_t workspace_bytes, cudaStream_t st) {
+int layer_norm_bwd_impl(const void* dy, int32_t dy_dtype, const float* x, const float* mean, const float* rstd,
+                        const float* gamma, int64_t M, int64_t N, float* dx, float* dgamma, float* dbeta,
+                        void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  TDX_CHECK_ARG(dy_dtype == TAU_DXB_F32 || dy_dtype == TAU_DXB_BF16, "layer norm: dy must be fp32 or bf16");
   TDX_CHECK_ARG(M >= 0 && N > 0 && N % 128 == 0 && N <= 1024,
                 "layer norm: need d a multiple of 128 up to 1024 (got %lld)", (long long)N);
   TDX_CHECK_ARG(dgamma && dbeta, "layer norm: null pointer");
@@ -244,7 +276,8 @@ int layer_norm_bwd_impl(const float* dy, const float* x, const float* mean, cons
   const int parts = ln_parts(M);
   float* pdg = static_cast<float*>(workspace);
   float* pdb = pdg + static_cast<size_t>(parts) * N;
-  int rc = dispatch_nch<BwdLaunch>(static_cast<int>(N), dy, x, mean, rstd, gamma, M, dx, pdg, pdb, parts, st);
+  int rc = dispatch_nch<BwdLaunch>(static_cast<int>(N), dy, static_cast<int>(dy_dtype == TAU_DXB_BF16), x, mean,
+                                   rstd, gamma, M, dx, pdg, pdb, parts, st);
   if (rc) return rc;
   const int threads = 256, blocks = static_cast<int>((2 * N + threads - 1) / threads);
   ln_bwd_reduce_kernel<<<blocks, threads, 0, st>>>(pdg, pdb, parts, static_cast<int>(N), dgamma, dbeta);

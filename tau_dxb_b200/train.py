@@ -100,9 +100,18 @@ def build_model(cfg: StepConfig, device, tau_init=None):
                              decoder_mode="sparse_grad", learnable_k=True,
                              init_k_ratio=cfg.init_k_ratio, track_wins=True)
     model._tau_dxb_encoder_hook = contiguous_encoder_stream(model)
-    LN.patch_layer_norms(model)
+    LN.patch_layer_norms(model, bf16_out=single_gemm_norm)
     model.train()
     return model
+
+
+def single_gemm_norm(name: str) -> bool:
+    """Norms of the patched Whisper whose output feeds one GEMM: each layer's
+    self-attention norm (the fused q/k/v projection), cross-attention norm
+    (q_proj), final norm (fc1), and the decoder's last norm (the LM head).
+    The encoder's last norm feeds every cross-attention k/v projection."""
+    return name.endswith(("self_attn_layer_norm", "encoder_attn_layer_norm", "final_layer_norm")) \
+        or name.endswith("decoder.layer_norm")
 
 
 def contiguous_encoder_stream(model):

@@ -73,11 +73,13 @@ def test_validation_without_gpu(C):
     assert lib.tau_star_analytic(None, 4, 64, 64, 9, None, None) == C.ERR_INVALID_ARGUMENT
     assert lib.tau_star_analytic(None, 4, 64, 64, 0, None, None) == C.ERR_INVALID_ARGUMENT
     assert lib.tau_star_analytic(None, 0, 64, 64, 0, None, None) == C.OK
-    assert lib.tau_layer_norm_fwd(None, 8, 100, None, None, 1e-5, None, None, None, None) == \
+    assert lib.tau_layer_norm_fwd(None, 8, 100, None, None, 1e-5, None, C.F32, None, None, None) == \
         C.ERR_INVALID_ARGUMENT
-    assert lib.tau_layer_norm_fwd(None, 8, 768, None, None, 1e-5, None, None, None, None) == \
+    assert lib.tau_layer_norm_fwd(None, 8, 768, None, None, 1e-5, None, C.F32, None, None, None) == \
         C.ERR_INVALID_ARGUMENT
-    assert lib.tau_layer_norm_fwd(None, 0, 768, None, None, 1e-5, None, None, None, None) == C.OK
+    assert lib.tau_layer_norm_fwd(None, 8, 768, None, None, 1e-5, None, C.F16, None, None, None) == \
+        C.ERR_INVALID_ARGUMENT
+    assert lib.tau_layer_norm_fwd(None, 0, 768, None, None, 1e-5, None, C.BF16, None, None, None) == C.OK
     assert lib.tau_layer_norm_bwd_workspace_bytes(24000, 768) >= 768 * 8
 
 

@@ -77,3 +77,36 @@ def test_patched_norm_under_autocast_returns_fp32_like_torch():
     assert rel_err(ln(xf).detach().cpu().numpy(), ref.detach().cpu().numpy()) < 2e-6
     LN.unpatch_layer_norms(ln)
     assert "forward" not in ln.__dict__
+
+
+@pytest.mark.parametrize("M,d", [(24000, 768), (37, 384)])
+def test_layer_norm_bf16_output_and_gradient(M, d):
+    """bf16 y is torch's fp32 norm rounded to bf16 (to 1 ulp where the two
+    fp32 results straddle a rounding boundary, in under 0.1% of elements); a
+    bf16 dy gives torch's dx,
+    dgamma, dbeta for that dy in fp32."""
+    from tau_dxb_b200 import layernorm as LN
+    g = torch.Generator(device="cuda").manual_seed(7 * M + d)
+    x = torch.randn(M, d, device="cuda", generator=g) * 2.0 - 0.5
+    w = torch.randn(d, device="cuda", generator=g)
+    b = torch.randn(d, device="cuda", generator=g)
+    dy = torch.randn(M, d, device="cuda", generator=g).to(torch.bfloat16)
+    ry, rdx, rdw, rdb = _ref(x, w, b, dy.float(), 1e-5)
+    xs = x.clone().requires_grad_()
+    ws = w.clone().requires_grad_()
+    bs = b.clone().requires_grad_()
+    y = LN.fused_layer_norm(xs, ws, bs, 1e-5, out_bf16=True)
+    assert y.dtype == torch.bfloat16
+    ref_b = ry.to(torch.bfloat16)
+    diff = (y.float() - ref_b.float()).abs()
+    # one bf16 ulp, plus 1e-5 absolute where y = xhat gamma + beta cancels to
+    # near zero and the two fp32 results differ by ~1e-7 before rounding
+    ulp = ref_b.float().abs() * 2.0 ** -7 + 1e-5
+    assert bool((diff <= ulp).all()), float((diff / ulp).max())
+    assert float((diff > 0).float().mean()) < 1e-3
+    y.backward(dy)
+    f = lambda t: t.detach().cpu().numpy()
+    assert rel_err(f(xs.grad), f(rdx)) < 2e-5
+    assert rel_err(f(ws.grad), f(rdw)) < 2e-5
+    assert rel_err(f(bs.grad), f(rdb)) < 2e-5
+
