@@ -385,7 +385,38 @@ def wta_sub_bench(torch, device, iters=20, warm=3):
     return res
 
 
-def train_sub_bench(torch, device, world, rank, steps=10, warmup=3):
+def write_step_profile(torch, step, batch, path):
+    """One train step under torch.profiler: ops by self device time, and for
+    every copy kernel over 20 us the chain of ops that launched it."""
+    import collections
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
+        step.step(*batch)
+        torch.cuda.synchronize()
+    lines = ["# self device time (us), calls, op / kernel"]
+    for e in sorted(prof.key_averages(), key=lambda e: -e.self_device_time_total)[:40]:
+        lines.append(f"{e.self_device_time_total:10.0f} {e.count:5d} {e.key[:160]}")
+    lines.append("# copy_ by caller chain: device time (us), calls, chain | shapes")
+    agg, tim = collections.Counter(), collections.Counter()
+    for ev in prof.events():
+        if ev.name == "aten::copy_" and ev.device_time_total > 20:
+            chain, p = [], ev.cpu_parent
+            while p is not None and len(chain) < 5:
+                chain.append(p.name)
+                p = p.cpu_parent
+            key = " <- ".join(chain) + " | " + str(ev.input_shapes)[:80]
+            agg[key] += 1
+            tim[key] += ev.device_time_total
+    for k, v in tim.most_common(25):
+        lines.append(f"{v:10.0f} {agg[k]:4d} {k}")
+    total = sum(e.self_device_time_total for e in prof.key_averages() if e.device_type.name == "CUDA")
+    lines.append(f"# total kernel time (us): {total:.0f}")
+    with open(path, "w") as f:
+        f.write("\n".join(lines) + "\n")
+
+
+def train_sub_bench(torch, device, world, rank, steps=10, warmup=3, profile_path=""):
     """Whisper-small tau-opus + WTA train step (batch 16 per GPU, bf16 autocast,
     fp32 master weights, AdamW); DDP + NCCL all-reduce when world > 1.
     samples/s of the whole job, max-over-ranks CUDA-event time."""
@@ -415,6 +446,8 @@ def train_sub_bench(torch, device, world, rank, steps=10, warmup=3):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    if profile_path and rank == 0:
+        write_step_profile(torch, step, batches[0], profile_path)
     flops = T.model_flops_per_step(cfg)
     peak = load_peaks()[2]
     out = {"samples_per_s": round(world * cfg.batch / (ms * 1e-3), 2), "ms_per_step": round(ms, 2),
@@ -733,6 +766,9 @@ def main():
                     help="only the tau* solver sub-benchmark (JSON of its results; for ncu captures)")
     ap.add_argument("--train-only", action="store_true",
                     help="only the Whisper train-step sub-benchmark (JSON of its results; for ncu launch lists)")
+    ap.add_argument("--torch-profile", default="",
+                    help="with --train-only: profile one more step with torch.profiler and write its top "
+                         "device-time ops and the callers of its copy kernels to this file")
     args = ap.parse_args()
     if args.profile_batch:
         args.quick = args.no_e2e = args.no_cpu = args.no_train = True
@@ -759,7 +795,8 @@ def main():
     if args.train_only:
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
-        ts = train_sub_bench(torch, device, world, rank, steps=args.steps, warmup=args.warmup)
+        ts = train_sub_bench(torch, device, world, rank, steps=args.steps, warmup=args.warmup,
+                             profile_path=args.torch_profile)
         if rank == 0:
             _emit(json.dumps({"train_step": ts}), json_fd)
         if world > 1:

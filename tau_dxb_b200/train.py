@@ -241,8 +241,36 @@ class TrainStep:
         self.sched = torch.optim.lr_scheduler.LambdaLR(
             self.opt, lr_lambda=lr_lambda(cfg.warmup_steps, cfg.t0_steps, cfg.t_mult))
         self.ema = WeightEMA(self.model, cfg.ema_decay) if cfg.ema_decay > 0 else None
-        self.skipped = 0
+        self._skipped = 0
         self.micro = 0                  # micro-batches since the last optimiser step
+        # Non-finite steps are skipped without a host sync when AdamW is fused
+        # (it skips on the device given found_inf) and there is no
+        # accumulation: the host reads a step's flag one step later.
+        self.lagged = bool(self.opt.defaults.get("fused")) and cfg.grad_accum == 1
+        self._pending = None            # (pinned flag, event) of the last step, not yet settled
+        if self.lagged:
+            self._flag_host = torch.zeros(1, dtype=torch.float32).pin_memory()
+
+    @property
+    def skipped(self) -> int:
+        """Steps skipped for a non-finite loss (settles the last step first)."""
+        self.flush()
+        return self._skipped
+
+    def flush(self):
+        """Settle the last step: when its loss was finite, its LR-schedule step
+        and weight EMA; otherwise count it as skipped."""
+        if self._pending is None:
+            return
+        ev = self._pending
+        self._pending = None
+        ev.synchronize()
+        if float(self._flag_host[0]) > 0:
+            self._skipped += 1
+            return
+        self.sched.step()
+        if self.ema is not None:
+            self.ema.update()
 
     def loss(self, mel, labels):
         amp = torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.device.type == "cuda")
@@ -253,7 +281,11 @@ class TrainStep:
 
     def step(self, mel, labels):
         """One micro-batch: forward, backward (+ all-reduce); every grad_accum
-        micro-batches clip, AdamW, LR schedule and EMA. Returns the loss."""
+        micro-batches clip, AdamW, LR schedule and EMA. Returns the loss.
+        A step whose loss is not finite (on any rank) changes nothing: no
+        AdamW update, no LR-schedule step, no EMA update."""
+        if self.lagged:
+            return self._step_lagged(mel, labels)
         import contextlib
         accumulate = self.world > 1 and self.micro + 1 < self.cfg.grad_accum
         with self.net.no_sync() if accumulate else contextlib.nullcontext():   # all-reduce on the last
@@ -265,7 +297,7 @@ class TrainStep:
         if float(bad.item()) > 0:       # every rank skips together
             self.opt.zero_grad(set_to_none=True)
             self.micro = 0
-            self.skipped += 1
+            self._skipped += 1
             return loss.detach()
         self.micro += 1
         if self.micro < self.cfg.grad_accum:
@@ -277,6 +309,32 @@ class TrainStep:
         self.opt.zero_grad(set_to_none=True)
         if self.ema is not None:
             self.ema.update()
+        return loss.detach()
+
+
+    def _step_lagged(self, mel, labels):
+        """The same step without waiting for the GPU. The non-finite flag goes
+        to AdamW as found_inf (the fused kernel leaves weights, moments and step
+        counts alone when it is set) and to pinned host memory. The host reads
+        it one step later, when this step's work has long finished while the
+        next step's is queued. At that point (before the next AdamW update, so
+        the weights are still this step's) it runs this step's LR-schedule
+        step and EMA update, or counts the skip. Same results as checking at
+        once; the GPU queue never drains."""
+        loss, _ = self.loss(mel, labels)
+        loss.backward()
+        bad = (~torch.isfinite(loss.detach())).float().reshape(())    # 0-dim, like AdamW's step counts
+        if self.world > 1:
+            dist.all_reduce(bad, op=dist.ReduceOp.MAX)     # exactly 1.0 when any rank is bad
+        self.flush()                     # the previous step: schedule and EMA, or skip
+        torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.clip)
+        self.opt.found_inf = bad
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=True)
+        self._flag_host.copy_(bad, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._pending = ev
         return loss.detach()
 
 

@@ -130,3 +130,34 @@ def test_fused_qkv_projection_matches_separate_projections():
     for n in gf:
         assert rel_err(gf[n], gs[n]) < 3e-2, (n, rel_err(gf[n], gs[n]))
 
+
+def test_lagged_nonfinite_skip_matches_synchronous_skip():
+    """The train step that reads its non-finite flag one step late (fused
+    AdamW skipping on the device) against the step that checks at once: over
+    good, good, NaN, good batches both skip exactly one step, leave the LR
+    schedule and the EMA at the same point, and end at the same weights (up to
+    the attention backward's reduction order)."""
+    from tau_dxb_b200 import train as T
+    cfg = tiny_cfg(batch=2, warmup_steps=2)
+    g = torch.Generator().manual_seed(21)
+    batches = [T.synthetic_batch(cfg, "cuda", g) for _ in range(4)]
+    bad_mel = batches[2][0].clone()
+    bad_mel[0, 0, 0] = float("nan")
+    batches[2] = (bad_mel, batches[2][1])
+    runs = []
+    for lagged in (True, False):
+        step = T.TrainStep(cfg, "cuda")
+        assert step.lagged                       # CUDA, fused AdamW, no accumulation
+        step.lagged = lagged
+        losses = [float(step.step(m, l)) for m, l in batches]
+        runs.append((step.skipped, step.sched.last_epoch, losses,
+                     {n: p.detach().float().cpu() for n, p in step.model.named_parameters()},
+                     [t.float().cpu() for t in step.ema.shadow]))
+    (sk_a, ep_a, lo_a, pa, ea), (sk_b, ep_b, lo_b, pb, eb) = runs
+    assert sk_a == sk_b == 1 and ep_a == ep_b == 3
+    assert not torch.isfinite(torch.tensor(lo_a[2])) and torch.isfinite(torch.tensor([lo_a[i] for i in (0, 1, 3)])).all()
+    for n in pa:
+        assert rel_err(pa[n], pb[n]) < 1e-3, (n, rel_err(pa[n], pb[n]))
+    for a, b in zip(ea, eb):
+        assert rel_err(a, b) < 1e-3
+
