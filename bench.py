@@ -386,14 +386,23 @@ def wta_sub_bench(torch, device, iters=20, warm=3):
 
 
 def write_step_profile(torch, step, batch, path):
-    """One train step under torch.profiler: ops by self device time, and for
-    every copy kernel over 20 us the chain of ops that launched it."""
+    """One eager train step under torch.profiler: ops by self device time,
+    and for every copy kernel over 20 us the chain of ops that launched it."""
     import collections
     from torch.profiler import ProfilerActivity, profile
+    # an eager step (a graph replay hides its kernels): the graph's gradient
+    # buffers are released first and the graph is captured again afterwards
+    graphed = getattr(step, "graphed", False)
+    if graphed:
+        step.opt.zero_grad(set_to_none=True)
+        step.graphed = False
     torch.cuda.synchronize()
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
         step.step(*batch)
         torch.cuda.synchronize()
+    if graphed:
+        step.graphed = True
+        step.reset_graph()
     lines = ["# self device time (us), calls, op / kernel"]
     for e in sorted(prof.key_averages(), key=lambda e: -e.self_device_time_total)[:40]:
         lines.append(f"{e.self_device_time_total:10.0f} {e.count:5d} {e.key[:160]}")

@@ -166,14 +166,21 @@ class WeightEMA:
         return dict(zip(self.names, self.shadow))
 
 
-def make_optimizer(model, cfg: StepConfig):
-    """AdamW with the reference's groups (echo/train_echo_opus1.py:344-355)."""
+def make_optimizer(model, cfg: StepConfig, capturable: bool = False):
+    """AdamW with the reference's groups (echo/train_echo_opus1.py:344-355).
+    capturable: fused AdamW whose step can be recorded in a CUDA graph, with
+    the learning rates as device tensors (the LR schedule fills them)."""
     base, taup = [], []
     for name, p in model.named_parameters():
         if not p.requires_grad:
             continue
         (taup if ("log_tau" in name or "log_alpha" in name) else base).append(p)
     fused = all(p.is_cuda for p in base + taup)
+    if capturable and fused:
+        dev = base[0].device
+        return torch.optim.AdamW([{"params": base, "lr": torch.tensor(cfg.lr, device=dev)},
+                                  {"params": taup, "lr": torch.tensor(cfg.tau_lr, device=dev)}],
+                                 weight_decay=cfg.weight_decay, fused=True, capturable=True)
     return torch.optim.AdamW([{"params": base, "lr": cfg.lr}, {"params": taup, "lr": cfg.tau_lr}],
                              weight_decay=cfg.weight_decay, fused=fused)
 
@@ -209,13 +216,29 @@ class PaddedHeadLoss(torch.nn.Module):
         bias = torch.zeros(v + self.pad)
         bias[v:] = float("-inf")
         self.register_buffer("head_bias", bias, persistent=False)
+        self._mask_key, self._mask = None, None
+
+    def causal_mask(self, B, L, device):
+        """[B, 1, L, L] additive causal mask with the values transformers builds
+        for eager attention (0 where key <= query, fp32 min above), made once
+        per shape. The decoder takes a ready 4D mask as it is, so no mask is
+        built inside the step (nor a host-to-device scalar copy)."""
+        key = (B, L, str(device))
+        if self._mask_key != key:
+            i = torch.arange(L, device=device)
+            m = torch.where(i[None, :] <= i[:, None], 0.0, torch.finfo(torch.float32).min)
+            self._mask = m.expand(B, 1, L, L)
+            self._mask_key = key
+        return self._mask
 
     def forward(self, input_features, labels):
         from transformers.models.whisper.modeling_whisper import shift_tokens_right
         cfg = self.whisper.config
         dec_in = shift_tokens_right(labels, cfg.pad_token_id, cfg.decoder_start_token_id)
         # no KV cache in training (it would copy every decoder layer's keys and values)
-        h = self.whisper.model(input_features, decoder_input_ids=dec_in, use_cache=False).last_hidden_state
+        mask = self.causal_mask(dec_in.shape[0], dec_in.shape[1], dec_in.device)
+        h = self.whisper.model(input_features, decoder_input_ids=dec_in, decoder_attention_mask=mask,
+                               use_cache=False).last_hidden_state
         w = self.whisper.proj_out.weight
         if self.pad:
             w = torch.nn.functional.pad(w, (0, 0, 0, self.pad))
@@ -226,7 +249,7 @@ class PaddedHeadLoss(torch.nn.Module):
 class TrainStep:
     """One fine-tune step on this rank (DDP-wrapped when a process group exists)."""
 
-    def __init__(self, cfg: StepConfig, device, tau_init=None, bucket_mb: int = 64):
+    def __init__(self, cfg: StepConfig, device, tau_init=None, bucket_mb: int = 64, cuda_graph: bool = True):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = build_model(cfg, self.device, tau_init)
@@ -237,9 +260,14 @@ class TrainStep:
             self.net = DDP(self.net, device_ids=[self.device.index] if self.device.type == "cuda" else None,
                            bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True,
                            broadcast_buffers=False)
-        self.opt = make_optimizer(self.model, cfg)
+        # one CUDA graph pair for the whole step: single GPU, no accumulation
+        self.graphed = bool(cuda_graph) and self.device.type == "cuda" and self.world == 1 and cfg.grad_accum == 1
+        self.opt = make_optimizer(self.model, cfg, capturable=self.graphed)
         self.sched = torch.optim.lr_scheduler.LambdaLR(
             self.opt, lr_lambda=lr_lambda(cfg.warmup_steps, cfg.t0_steps, cfg.t_mult))
+        # float base rates: the schedule then fills the tensor rates of a
+        # capturable AdamW without reading a device value back
+        self.sched.base_lrs = [cfg.lr, cfg.tau_lr]
         self.ema = WeightEMA(self.model, cfg.ema_decay) if cfg.ema_decay > 0 else None
         self._skipped = 0
         self.micro = 0                  # micro-batches since the last optimiser step
@@ -250,7 +278,16 @@ class TrainStep:
         self._pending = None            # (pinned flag, event) of the last step, not yet settled
         if self.lagged:
             self._flag_host = torch.zeros(1, dtype=torch.float32).pin_memory()
+        self.graph_warmup = 2           # eager steps (on a side stream) before the capture
+        self.reset_graph()
 
+    def reset_graph(self):
+        """Drop the captured step; the next calls warm up and capture again.
+        Needed after anything the capture froze changes: batch shapes, or the
+        sparse-grad patch's settings (k ratios, win collection, prune masks)."""
+        self._gA = self._gB = None
+        self._eager_calls = 0
+        self._static = None
     @property
     def skipped(self) -> int:
         """Steps skipped for a non-finite loss (settles the last step first)."""
@@ -284,6 +321,8 @@ class TrainStep:
         micro-batches clip, AdamW, LR schedule and EMA. Returns the loss.
         A step whose loss is not finite (on any rank) changes nothing: no
         AdamW update, no LR-schedule step, no EMA update."""
+        if self.graphed and self.lagged:
+            return self._step_graphed(mel, labels)
         if self.lagged:
             return self._step_lagged(mel, labels)
         import contextlib
@@ -336,6 +375,65 @@ class TrainStep:
         ev.record()
         self._pending = ev
         return loss.detach()
+
+
+    def _fwd_bwd(self, mel, labels):
+        """Forward, backward, clip; the non-finite flag as a 0-dim tensor."""
+        loss, _ = self.loss(mel, labels)
+        loss.backward()
+        bad = (~torch.isfinite(loss.detach())).float().reshape(())
+        torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.clip)
+        return loss.detach(), bad
+
+    def _post(self, bad):
+        self._flag_host.copy_(bad, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._pending = ev
+
+    def _step_graphed(self, mel, labels):
+        """The lagged step replayed from two CUDA graphs: A = forward, backward,
+        clip and flag; B = the AdamW update (found_inf = the flag). The previous
+        step is settled between them (host waits while A runs; its EMA reads
+        the weights before B changes them). The batch is copied into static
+        buffers. The first graph_warmup calls are ordinary steps on a side
+        stream; the next one captures both graphs, then replays them."""
+        if self._gA is None and self._eager_calls < self.graph_warmup:
+            self._eager_calls += 1
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                loss, bad = self._fwd_bwd(mel, labels)
+                self.flush()
+                self.opt.found_inf = bad
+                self.opt.step()
+                self.opt.zero_grad(set_to_none=True)
+                self._post(bad)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            return loss
+        if self._gA is None:
+            self.flush()
+            torch.cuda.synchronize(self.device)
+            self._static = (mel.clone(), labels.clone())
+            self.opt.zero_grad(set_to_none=True)
+            gA, gB = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gA):
+                self._sloss, self._sbad = self._fwd_bwd(*self._static)
+            self.opt.found_inf = self._sbad
+            with torch.cuda.graph(gB, pool=gA.pool()):
+                self.opt.step()
+            self._gA, self._gB = gA, gB
+        smel, slab = self._static
+        if mel.shape != smel.shape or labels.shape != slab.shape:
+            raise ValueError("TrainStep: batch shapes changed since the CUDA graph was captured "
+                             f"({tuple(smel.shape)}, {tuple(slab.shape)}); call reset_graph()")
+        smel.copy_(mel, non_blocking=True)
+        slab.copy_(labels, non_blocking=True)
+        self._gA.replay()
+        self.flush()
+        self._gB.replay()
+        self._post(self._sbad)
+        return self._sloss.clone()
 
 
 def model_flops_per_step(cfg: StepConfig) -> float:

@@ -131,33 +131,42 @@ def test_fused_qkv_projection_matches_separate_projections():
         assert rel_err(gf[n], gs[n]) < 3e-2, (n, rel_err(gf[n], gs[n]))
 
 
-def test_lagged_nonfinite_skip_matches_synchronous_skip():
-    """The train step that reads its non-finite flag one step late (fused
-    AdamW skipping on the device) against the step that checks at once: over
-    good, good, NaN, good batches both skip exactly one step, leave the LR
-    schedule and the EMA at the same point, and end at the same weights (up to
-    the attention backward's reduction order)."""
+def test_lagged_and_graphed_steps_match_synchronous_step():
+    """Three forms of the train step over good x4, NaN, good batches: the
+    synchronous check, the step that reads its non-finite flag one step late
+    (fused AdamW skipping on the device), and that step replayed from CUDA
+    graphs (two eager warm-up steps, capture on the third). All skip exactly
+    one step, leave the LR schedule and the EMA at the same point, and end at
+    the same weights (up to the attention backward's reduction order)."""
     from tau_dxb_b200 import train as T
     cfg = tiny_cfg(batch=2, warmup_steps=2)
     g = torch.Generator().manual_seed(21)
-    batches = [T.synthetic_batch(cfg, "cuda", g) for _ in range(4)]
-    bad_mel = batches[2][0].clone()
+    batches = [T.synthetic_batch(cfg, "cuda", g) for _ in range(6)]
+    bad_mel = batches[4][0].clone()
     bad_mel[0, 0, 0] = float("nan")
-    batches[2] = (bad_mel, batches[2][1])
-    runs = []
-    for lagged in (True, False):
-        step = T.TrainStep(cfg, "cuda")
-        assert step.lagged                       # CUDA, fused AdamW, no accumulation
-        step.lagged = lagged
+    batches[4] = (bad_mel, batches[4][1])
+    runs = {}
+    for mode in ("sync", "lagged", "graph"):
+        step = T.TrainStep(cfg, "cuda", cuda_graph=(mode == "graph"))
+        assert step.lagged and step.graphed == (mode == "graph")
+        step.lagged = mode != "sync"
         losses = [float(step.step(m, l)) for m, l in batches]
-        runs.append((step.skipped, step.sched.last_epoch, losses,
-                     {n: p.detach().float().cpu() for n, p in step.model.named_parameters()},
-                     [t.float().cpu() for t in step.ema.shadow]))
-    (sk_a, ep_a, lo_a, pa, ea), (sk_b, ep_b, lo_b, pb, eb) = runs
-    assert sk_a == sk_b == 1 and ep_a == ep_b == 3
-    assert not torch.isfinite(torch.tensor(lo_a[2])) and torch.isfinite(torch.tensor([lo_a[i] for i in (0, 1, 3)])).all()
-    for n in pa:
-        assert rel_err(pa[n], pb[n]) < 1e-3, (n, rel_err(pa[n], pb[n]))
-    for a, b in zip(ea, eb):
-        assert rel_err(a, b) < 1e-3
-
+        if mode == "graph":
+            assert step._gA is not None
+        runs[mode] = (step.skipped, step.sched.last_epoch, losses,
+                      {n: p.detach().float().cpu() for n, p in step.model.named_parameters()},
+                      [t.float().cpu() for t in step.ema.shadow],
+                      [float(gr["lr"]) for gr in step.opt.param_groups])
+    sk, ep, lo, pr, em, lr = runs["sync"]
+    assert sk == 1 and ep == 5
+    assert not torch.isfinite(torch.tensor(lo[4]))
+    for mode in ("lagged", "graph"):
+        sk2, ep2, lo2, pr2, em2, lr2 = runs[mode]
+        assert (sk2, ep2) == (sk, ep), mode
+        assert lr2 == pytest.approx(lr, rel=1e-6), mode
+        for i in (0, 1, 2, 3, 5):
+            assert abs(lo2[i] - lo[i]) <= 1e-3 * abs(lo[i]), (mode, i, lo2[i], lo[i])
+        for n in pr:
+            assert rel_err(pr2[n], pr[n]) < 1e-3, (mode, n, rel_err(pr2[n], pr[n]))
+        for a, b in zip(em2, em):
+            assert rel_err(a, b) < 1e-3, mode
