@@ -298,6 +298,20 @@ TAU_DXB_API int tau_layer_norm_bwd(const void* dy, int32_t dy_dtype, const float
                                    int64_t M, int64_t d, float* dx, float* dgamma, float* dbeta,
                                    void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Column sums of a row-major [M, N] matrix, out[n] = sum_m x[m, n], fp32
+ * accumulation in a fixed order (the same bits on every call): the bias
+ * gradient of the linear layers of the Whisper model that
+ * echo/train_echo_opus1.py:405-434 trains (autograd's grad_output.sum(0)).
+ * x: bf16 or fp32 (dtype), 16-byte aligned, N a multiple of 8; out: N
+ * values of out_dtype (bf16 or fp32). workspace: device memory of
+ * tau_column_sum_workspace_bytes(M, N) bytes, 4-byte aligned.
+ */
+TAU_DXB_API size_t tau_column_sum_workspace_bytes(int64_t M, int64_t N);
+TAU_DXB_API int tau_column_sum(const void* x, int32_t dtype, int64_t M, int64_t N, void* out,
+                               int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

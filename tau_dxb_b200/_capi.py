@@ -79,6 +79,8 @@ SIGNATURES = {
     "tau_layer_norm_bwd_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "tau_layer_norm_bwd": (ctypes.c_int, [_vp, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp,
                                           ctypes.c_size_t, _vp]),
+    "tau_column_sum_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
+    "tau_column_sum": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _i32, _vp, ctypes.c_size_t, _vp]),
 }
 
 _lib = None

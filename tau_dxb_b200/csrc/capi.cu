@@ -56,6 +56,8 @@ int tau_star_solve_impl(const float*, int64_t, int64_t, int64_t, int32_t, int32_
                         float*, float*, cudaStream_t);
 int tau_star_analytic_impl(const float*, int64_t, int64_t, int64_t, int32_t, float*, cudaStream_t);
 size_t layer_norm_bwd_workspace(int64_t M, int64_t N);
+size_t column_sum_workspace(int64_t M, int64_t N);
+int column_sum_impl(const void*, int32_t, int64_t, int64_t, void*, int32_t, void*, size_t, cudaStream_t);
 int layer_norm_fwd_impl(const float*, int64_t, int64_t, const float*, const float*, float, void*, int32_t, float*,
                         float*, cudaStream_t);
 int layer_norm_bwd_impl(const void*, int32_t, const float*, const float*, const float*, const float*, int64_t,
@@ -268,6 +270,15 @@ int tau_layer_norm_bwd(const void* dy, int32_t dy_dtype, const float* x, const f
   g_last_error[0] = 0;
   return layer_norm_bwd_impl(dy, dy_dtype, x, mean, rstd, gamma, M, d, dx, dgamma, dbeta, workspace,
                              workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t tau_column_sum_workspace_bytes(int64_t M, int64_t N) { return column_sum_workspace(M, N); }
+
+int tau_column_sum(const void* x, int32_t dtype, int64_t M, int64_t N, void* out, int32_t out_dtype,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error[0] = 0;
+  return column_sum_impl(x, dtype, M, N, out, out_dtype, workspace, workspace_bytes,
+                         static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

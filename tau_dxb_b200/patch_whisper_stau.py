@@ -180,15 +180,16 @@ def _fused_projections(self, hidden_states, key_value_states):
     cast to bf16 once under autocast, and its gradient comes back as one
     tensor instead of three cast back to fp32 and added. Parameters stay
     separate (same state_dict); the outputs are strided views of one buffer."""
+    from .linear import linear
     wq, wk, wv = self.q_proj.weight, self.k_proj.weight, self.v_proj.weight
     if key_value_states is None:
         w = torch.cat([wq, wk, wv], 0)
         b = torch.cat([_proj_bias(self.q_proj, wq), _proj_bias(self.k_proj, wq), _proj_bias(self.v_proj, wq)])
-        return F.linear(hidden_states, w, b).split([wq.shape[0], wk.shape[0], wv.shape[0]], dim=-1)
+        return linear(hidden_states, w, b).split([wq.shape[0], wk.shape[0], wv.shape[0]], dim=-1)
     q = self.q_proj(hidden_states)
     w = torch.cat([wk, wv], 0)
     b = torch.cat([_proj_bias(self.k_proj, wk), _proj_bias(self.v_proj, wk)])
-    k, v = F.linear(key_value_states, w, b).split([wk.shape[0], wv.shape[0]], dim=-1)
+    k, v = linear(key_value_states, w, b).split([wk.shape[0], wv.shape[0]], dim=-1)
     return q, k, v
 
 

@@ -27,6 +27,7 @@ import torch
 import torch.distributed as dist
 
 from . import layernorm as LN
+from . import linear as LIN
 from . import patch_whisper_sparse_grad as SG
 from . import patch_whisper_stau as ST
 
@@ -101,6 +102,7 @@ def build_model(cfg: StepConfig, device, tau_init=None):
                              init_k_ratio=cfg.init_k_ratio, track_wins=True)
     model._tau_dxb_encoder_hook = contiguous_encoder_stream(model)
     LN.patch_layer_norms(model, bf16_out=single_gemm_norm)
+    LIN.patch_linears(model)
     model.train()
     return model
 

@@ -81,6 +81,10 @@ def test_validation_without_gpu(C):
         C.ERR_INVALID_ARGUMENT
     assert lib.tau_layer_norm_fwd(None, 0, 768, None, None, 1e-5, None, C.BF16, None, None, None) == C.OK
     assert lib.tau_layer_norm_bwd_workspace_bytes(24000, 768) >= 768 * 8
+    assert lib.tau_column_sum(None, C.BF16, 8, 100, None, C.BF16, None, 0, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_column_sum(None, C.F16, 8, 128, None, C.BF16, None, 0, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_column_sum(None, C.BF16, 8, 128, None, C.BF16, None, 0, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_column_sum_workspace_bytes(24000, 3072) >= 3072 * 4
 
 
 def test_workspace_size_formula(C):
