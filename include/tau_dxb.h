@@ -312,6 +312,23 @@ TAU_DXB_API int tau_column_sum(const void* x, int32_t dtype, int64_t M, int64_t 
                                int32_t out_dtype, void* workspace, size_t workspace_bytes,
                                void* stream);
 
+/*
+ * Cross-entropy over bf16 logits with fp32 math, the loss of
+ * echo/train_echo_opus1.py:405-420 (F.cross_entropy of the LM-head logits,
+ * labels == ignore_index not counted), without an fp32 copy of the logits.
+ * logits: bf16 [M, V] row-major, 16-byte aligned, V a multiple of 8;
+ * labels: int64 [M]. Forward writes loss_row[m] = logsumexp(x_m) - x_m[label]
+ * (0 for an ignored row, NaN for a label outside [0, V)) and lse[m]; the mean
+ * is loss_row summed / the number of counted rows. Backward writes
+ * dlogits = (softmax(x_m) - onehot(label)) * grad_scale[0] in bf16, 0 for
+ * ignored rows; grad_scale is a device fp32 scalar (dloss / counted rows).
+ */
+TAU_DXB_API int tau_cross_entropy_fwd(const void* logits, int64_t M, int64_t V, const int64_t* labels,
+                                      int64_t ignore_index, float* loss_row, float* lse, void* stream);
+TAU_DXB_API int tau_cross_entropy_bwd(const void* logits, int64_t M, int64_t V, const int64_t* labels,
+                                      int64_t ignore_index, const float* lse, const float* grad_scale,
+                                      void* dlogits, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -58,6 +58,9 @@ int tau_star_analytic_impl(const float*, int64_t, int64_t, int64_t, int32_t, flo
 size_t layer_norm_bwd_workspace(int64_t M, int64_t N);
 size_t column_sum_workspace(int64_t M, int64_t N);
 int column_sum_impl(const void*, int32_t, int64_t, int64_t, void*, int32_t, void*, size_t, cudaStream_t);
+int cross_entropy_fwd_impl(const void*, int64_t, int64_t, const int64_t*, int64_t, float*, float*, cudaStream_t);
+int cross_entropy_bwd_impl(const void*, int64_t, int64_t, const int64_t*, int64_t, const float*, const float*, void*,
+                           cudaStream_t);
 int layer_norm_fwd_impl(const float*, int64_t, int64_t, const float*, const float*, float, void*, int32_t, float*,
                         float*, cudaStream_t);
 int layer_norm_bwd_impl(const void*, int32_t, const float*, const float*, const float*, const float*, int64_t,
@@ -279,6 +282,19 @@ int tau_column_sum(const void* x, int32_t dtype, int64_t M, int64_t N, void* out
   g_last_error[0] = 0;
   return column_sum_impl(x, dtype, M, N, out, out_dtype, workspace, workspace_bytes,
                          static_cast<cudaStream_t>(stream));
+}
+
+int tau_cross_entropy_fwd(const void* logits, int64_t M, int64_t V, const int64_t* labels, int64_t ignore_index,
+                          float* loss_row, float* lse, void* stream) {
+  g_last_error[0] = 0;
+  return cross_entropy_fwd_impl(logits, M, V, labels, ignore_index, loss_row, lse, static_cast<cudaStream_t>(stream));
+}
+
+int tau_cross_entropy_bwd(const void* logits, int64_t M, int64_t V, const int64_t* labels, int64_t ignore_index,
+                          const float* lse, const float* grad_scale, void* dlogits, void* stream) {
+  g_last_error[0] = 0;
+  return cross_entropy_bwd_impl(logits, M, V, labels, ignore_index, lse, grad_scale, dlogits,
+                                static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

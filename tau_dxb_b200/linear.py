@@ -7,6 +7,11 @@ through torch's generic reduction, which runs bf16 column sums at ~1.6 TB/s
 under autocast's bf16 policy) and the dX / dW GEMMs, and sums the columns
 with one HBM sweep instead. ``patch_linears(model)`` routes every nn.Linear
 of a CUDA model through it; ``linear`` is the function form.
+
+``cross_entropy`` is the train step's loss on bf16 logits: autocast runs
+F.cross_entropy in fp32, which first copies the [tokens, vocab] logits to
+fp32 (1.5 GB per Whisper-small step) and casts the gradient back; the fused
+kernels read the bf16 logits directly (fp32 math) and write a bf16 gradient.
 """
 from __future__ import annotations
 
@@ -81,3 +86,46 @@ def patch_linears(model) -> int:
             m.forward = types.MethodType(_forward, m)
             n += 1
     return n
+
+
+class CrossEntropyFunction(torch.autograd.Function):
+    """Mean cross-entropy of bf16 logits [M, V] against int64 labels [M]
+    (ignore_index rows not counted), fp32 math, no fp32 copy of the logits."""
+
+    @staticmethod
+    def forward(ctx, logits, labels, ignore_index):
+        M, V = logits.shape
+        loss_row = torch.empty(M, dtype=torch.float32, device=logits.device)
+        lse = torch.empty_like(loss_row)
+        rc = C.lib().tau_cross_entropy_fwd(logits.data_ptr(), M, V, labels.data_ptr(), int(ignore_index),
+                                           loss_row.data_ptr(), lse.data_ptr(), C.stream_ptr(logits.device))
+        C.check("tau_cross_entropy_fwd", rc)
+        counted = (labels != ignore_index).sum().to(torch.float32)
+        ctx.save_for_backward(logits, labels, lse, counted)
+        ctx.ignore_index = int(ignore_index)
+        return loss_row.sum() / counted
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, labels, lse, counted = ctx.saved_tensors
+        M, V = logits.shape
+        scale = (g.float() / counted).reshape(1).contiguous()
+        dlogits = torch.empty_like(logits)
+        rc = C.lib().tau_cross_entropy_bwd(logits.data_ptr(), M, V, labels.data_ptr(), ctx.ignore_index,
+                                           lse.data_ptr(), scale.data_ptr(), dlogits.data_ptr(),
+                                           C.stream_ptr(logits.device))
+        C.check("tau_cross_entropy_bwd", rc)
+        return dlogits, None, None
+
+
+def cross_entropy(logits, labels, ignore_index: int = -100):
+    """F.cross_entropy(logits, labels) (mean, ignore_index) -- on the fused
+    kernels for contiguous bf16 CUDA logits with a width that is a multiple
+    of 8, else F.cross_entropy itself."""
+    if logits.is_cuda and logits.dtype == torch.bfloat16 and logits.dim() == 2 and logits.shape[1] % 8 == 0 \
+            and labels.dtype == torch.int64:
+        lg = logits.contiguous()
+        if lg.data_ptr() % 16 == 0:
+            return CrossEntropyFunction.apply(lg, labels.contiguous(), ignore_index)
+    return F.cross_entropy(logits, labels, ignore_index=ignore_index)
+

@@ -245,7 +245,7 @@ class PaddedHeadLoss(torch.nn.Module):
         if self.pad:
             w = torch.nn.functional.pad(w, (0, 0, 0, self.pad))
         logits = torch.nn.functional.linear(h, w, self.head_bias.to(w.dtype))
-        return torch.nn.functional.cross_entropy(logits.view(-1, logits.shape[-1]), labels.reshape(-1))
+        return LIN.cross_entropy(logits.view(-1, logits.shape[-1]), labels.reshape(-1))
 
 
 class TrainStep:

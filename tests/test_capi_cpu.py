@@ -85,6 +85,9 @@ def test_validation_without_gpu(C):
     assert lib.tau_column_sum(None, C.F16, 8, 128, None, C.BF16, None, 0, None) == C.ERR_INVALID_ARGUMENT
     assert lib.tau_column_sum(None, C.BF16, 8, 128, None, C.BF16, None, 0, None) == C.ERR_INVALID_ARGUMENT
     assert lib.tau_column_sum_workspace_bytes(24000, 3072) >= 3072 * 4
+    assert lib.tau_cross_entropy_fwd(None, 4, 100, None, -100, None, None, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_cross_entropy_fwd(None, 4, 128, None, -100, None, None, None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_cross_entropy_bwd(None, 0, 128, None, -100, None, None, None, None) == C.OK
 
 
 def test_workspace_size_formula(C):
