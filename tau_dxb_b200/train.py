@@ -419,8 +419,16 @@ class TrainStep:
             self._static = (mel.clone(), labels.clone())
             self.opt.zero_grad(set_to_none=True)
             gA, gB = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            tracker = SG._TRACKER
+            steps0 = dict(tracker.total_steps) if tracker is not None else {}
             with torch.cuda.graph(gA):
                 self._sloss, self._sbad = self._fwd_bwd(*self._static)
+            # Python-side counters the forward advanced while being captured
+            # (the win tracker's per-layer step counts): a replay does not run
+            # Python, so each later replay adds the same amounts
+            self._host_deltas = {k: v - steps0.get(k, 0) for k, v in tracker.total_steps.items()} \
+                if tracker is not None else {}
+            self._replays = 0
             self.opt.found_inf = self._sbad
             with torch.cuda.graph(gB, pool=gA.pool()):
                 self.opt.step()
@@ -431,6 +439,10 @@ class TrainStep:
                              f"({tuple(smel.shape)}, {tuple(slab.shape)}); call reset_graph()")
         smel.copy_(mel, non_blocking=True)
         slab.copy_(labels, non_blocking=True)
+        if self._replays and SG._TRACKER is not None:
+            for k, d in self._host_deltas.items():
+                SG._TRACKER.total_steps[k] += d
+        self._replays += 1
         self._gA.replay()
         self.flush()
         self._gB.replay()

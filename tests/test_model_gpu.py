@@ -153,6 +153,10 @@ def test_lagged_and_graphed_steps_match_synchronous_step():
         losses = [float(step.step(m, l)) for m, l in batches]
         if mode == "graph":
             assert step._gA is not None
+        # the win tracker's step counts advance on replayed steps too
+        from tau_dxb_b200 import patch_whisper_sparse_grad as SG
+        counts = SG._TRACKER.total_steps
+        assert counts and all(v == len(batches) for v in counts.values()), dict(counts)
         runs[mode] = (step.skipped, step.sched.last_epoch, losses,
                       {n: p.detach().float().cpu() for n, p in step.model.named_parameters()},
                       [t.float().cpu() for t in step.ema.shadow],
