@@ -263,7 +263,11 @@ class TrainStep:
                            bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True,
                            broadcast_buffers=False)
         # one CUDA graph pair for the whole step: single GPU, no accumulation
-        self.graphed = bool(cuda_graph) and self.device.type == "cuda" and self.world == 1 and cfg.grad_accum == 1
+        # (LayerDrop draws on the host in every forward, which a graph would freeze)
+        layerdrop = getattr(self.model.config, "encoder_layerdrop", 0.0) or getattr(self.model.config,
+                                                                                "decoder_layerdrop", 0.0)
+        self.graphed = bool(cuda_graph) and self.device.type == "cuda" and self.world == 1 \
+            and cfg.grad_accum == 1 and not layerdrop
         self.opt = make_optimizer(self.model, cfg, capturable=self.graphed)
         self.sched = torch.optim.lr_scheduler.LambdaLR(
             self.opt, lr_lambda=lr_lambda(cfg.warmup_steps, cfg.t0_steps, cfg.t_mult))
