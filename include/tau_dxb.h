@@ -65,6 +65,11 @@ extern "C" {
 /* ---- WTA modes ------------------------------------------------------------ */
 #define TAU_DXB_WTA_THRESHOLD 0 /* keep x >= k-th largest (ties keep more) */
 #define TAU_DXB_WTA_EXACT_K   1 /* keep exactly k; ties by lowest index    */
+#define TAU_DXB_WTA_GELU_INPUT 0x100 /* or'ed into the mode of wta_fwd: x is the
+                                        pre-activation, the select runs on
+                                        gelu(x) (erf form, bf16-rounded) and y
+                                        is gelu(x) where kept; bf16 rows of d a
+                                        multiple of 256, threshold mode, y given */
 
 /* Library version (major*10000 + minor*100 + patch). */
 TAU_DXB_API int tau_dxb_version(void);
@@ -211,6 +216,18 @@ TAU_DXB_API int wta_fwd(const void* x, int32_t dtype, int64_t n_rows, int64_t d,
  */
 TAU_DXB_API int wta_bwd(const void* dy, int32_t dtype, const uint8_t* bitmask,
             int64_t n_rows, int64_t d, void* dx, void* stream);
+
+/*
+ * Backward through GELU and WTA together, for a forward run with
+ * TAU_DXB_WTA_GELU_INPUT: dx = gelu'(x) * (dy * keep), with dy * keep rounded to
+ * bf16 and the GELU gradient in fp32 as PyTorch's bf16 GELU backward forms it.
+ * Replaces the WTA backward (echo/triton_wta.py:53-68) followed by the MLP's
+ * GELU backward in the encoder layers of echo/patch_whisper_sparse_grad.py.
+ * dy, x (the pre-activation), dx: bf16 [n_rows, d] contiguous, 16-byte
+ * aligned, d a multiple of 8; bitmask as wta_fwd.
+ */
+TAU_DXB_API int wta_bwd_gelu(const void* dy, const void* x, const uint8_t* bitmask, int64_t n_rows,
+                             int64_t d, void* dx, void* stream);
 
 /*
  * k for every learnable-k layer at once, on the device:

@@ -24,6 +24,7 @@ F32, BF16, F16 = 0, 1, 2
 SIGMA_IDS = {"softplus": 0, "sigmoid": 1, "exp": 2, "relu": 3}
 PATH_AUTO, PATH_PRECISE, PATH_TENSOR = 0, 1, 2
 WTA_THRESHOLD, WTA_EXACT_K = 0, 1
+WTA_GELU_INPUT = 0x100
 TAU_STAR_MAX_KEYS = 28672
 
 _i64p = ctypes.POINTER(ctypes.c_int64)
@@ -71,6 +72,7 @@ SIGNATURES = {
         _i32, _vp]),                                  # path, stream
     "wta_fwd": (ctypes.c_int, [_vp, _i32, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _vp]),
     "wta_bwd": (ctypes.c_int, [_vp, _i32, _vp, _i64, _i64, _vp, _vp]),
+    "wta_bwd_gelu": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _vp, _vp]),
     "wta_k_from_logits": (ctypes.c_int, [_vp, _i64, _i64, _vp, _vp]),
     "tau_star_solve": (ctypes.c_int, [_vp, _i64, _i64, _i64, _i32, _i32, ctypes.c_float, ctypes.c_float,
                                       ctypes.c_float, ctypes.c_float, _vp, _vp, _vp]),

@@ -49,6 +49,7 @@ int sm_count() {
 int wta_fwd_impl(const void*, int32_t, int64_t, int64_t, int64_t, int64_t, const int32_t*, int32_t,
                  void*, uint8_t*, int32_t*, cudaStream_t);
 int wta_bwd_impl(const void*, int32_t, const uint8_t*, int64_t, int64_t, void*, cudaStream_t);
+int wta_bwd_gelu_impl(const void*, const void*, const uint8_t*, int64_t, int64_t, void*, cudaStream_t);
 int wta_k_from_logits_impl(const float*, int64_t, int64_t, int32_t*, cudaStream_t);
 size_t whisper_log_mel_workspace(int64_t batch);
 int whisper_log_mel_impl(const float*, int64_t, int64_t, const float*, float*, void*, size_t, cudaStream_t);
@@ -227,6 +228,12 @@ int wta_bwd(const void* dy, int32_t dtype, const uint8_t* bitmask, int64_t n_row
             void* dx, void* stream) {
   g_last_error[0] = 0;
   return wta_bwd_impl(dy, dtype, bitmask, n_rows, d, dx, static_cast<cudaStream_t>(stream));
+}
+
+int wta_bwd_gelu(const void* dy, const void* x, const uint8_t* bitmask, int64_t n_rows, int64_t d, void* dx,
+                 void* stream) {
+  g_last_error[0] = 0;
+  return wta_bwd_gelu_impl(dy, x, bitmask, n_rows, d, dx, static_cast<cudaStream_t>(stream));
 }
 
 int wta_k_from_logits(const float* logits, int64_t n, int64_t d_ff, int32_t* k_out, void* stream) {

@@ -195,13 +195,34 @@ constexpr uint32_t kGallopMax = 64;
 
 template <bool B> struct BoolC { static constexpr bool value = B; };
 
+// GELU (erf form) as PyTorch's CUDA kernels evaluate it for bf16 tensors: fp32
+// math, y = (x * 0.5) * (1 + erf(x / sqrt(2))); gradient dy * (cdf + x * pdf)
+// with cdf = 0.5 (1 + erf(x / sqrt(2))), pdf = exp(-x^2 / 2) / sqrt(2 pi)
+__device__ __forceinline__ float gelu_erf(float x) {
+  constexpr float kAlpha = static_cast<float>(0.70710678118654752440);
+  return x * 0.5f * (1.f + erff(x * kAlpha));
+}
+__device__ __forceinline__ float gelu_erf_grad(float dy, float x) {
+  constexpr float kAlpha = static_cast<float>(0.70710678118654752440);
+  constexpr float kBeta = static_cast<float>(1.12837916709551257390 * 0.70710678118654752440 * 0.5);
+  const float cdf = 0.5f * (1.f + erff(x * kAlpha));
+  const float pdf = expf(-0.5f * x * x) * kBeta;
+  return dy * (cdf + x * pdf);
+}
+// two bf16 in a word -> gelu of each, rounded to nearest even
+__device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t w) {
+  const __nv_bfloat162 r = __floats2bfloat162_rn(gelu_erf(__uint_as_float(w << 16)),
+                                                 gelu_erf(__uint_as_float(w & 0xffff0000u)));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
 // Blocks per SM the register budget is sized for: two rows (this one and the
 // prefetched next) take 8*CH registers per thread.
-template <int CH, bool HIST>
-constexpr int fwd16_min_blocks() { return CH > 12 ? 2 : (CH == 12 && HIST ? 3 : 4); }
+template <int CH, bool HIST, bool GELU = false>
+constexpr int fwd16_min_blocks() { return CH > 12 ? 2 : (CH == 12 && (HIST || GELU) ? 3 : 4); }
 
-template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST>
-__global__ void __launch_bounds__(kFastWarps * 32, fwd16_min_blocks<CH, HIST>())
+template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST, bool GELU = false>
+__global__ void __launch_bounds__(kFastWarps * 32, fwd16_min_blocks<CH, HIST, GELU>())
 wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_stride,
                  int k_host, const int32_t* __restrict__ k_dev,
                  uint16_t* __restrict__ y, uint8_t* __restrict__ bitmask,
@@ -238,6 +259,12 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
     uint4 w[CH];
 #pragma unroll
     for (int c = 0; c < CH; ++c) w[c] = nxt[c];
+    if constexpr (GELU) {     // the row is the pre-activation: select on gelu(x)
+      static_assert(BF, "GELU input is bf16 only");
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        w[c] = make_uint4(gelu_bf16x2(w[c].x), gelu_bf16x2(w[c].y), gelu_bf16x2(w[c].z), gelu_bf16x2(w[c].w));
+    }
     // prefetch the next row while this one is selected
     const int64_t nrow = row + stride_rows;
     if (nrow < n_rows) {
@@ -492,6 +519,32 @@ wta_bwd_vec_kernel(const T* __restrict__ dy, const uint8_t* __restrict__ mask,
   }
 }
 
+// Backward through GELU then WTA (bf16): dx = gelu'(x) * (dy * keep), each
+// factor as PyTorch forms it (dy * keep in bf16, then the GELU gradient in fp32).
+__global__ void __launch_bounds__(256)
+wta_bwd_gelu_vec_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                        const uint8_t* __restrict__ mask, __nv_bfloat16* __restrict__ dx, int64_t n_bytes) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_bytes;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t m = mask[i];
+    const uint4 gv = __ldcs(reinterpret_cast<const uint4*>(dy) + i);
+    const uint4 xv = __ldcs(reinterpret_cast<const uint4*>(x) + i);
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float g0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(gw[j] << 16) *
+                                                            (((m >> (2 * j)) & 1u) ? 1.f : 0.f)));
+      const float g1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(gw[j] & 0xffff0000u) *
+                                                            (((m >> (2 * j + 1)) & 1u) ? 1.f : 0.f)));
+      const __nv_bfloat162 r = __floats2bfloat162_rn(gelu_erf_grad(g0, __uint_as_float(xw[j] << 16)),
+                                                     gelu_erf_grad(g1, __uint_as_float(xw[j] & 0xffff0000u)));
+      o[j] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+    __stcs(reinterpret_cast<uint4*>(dx) + i, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
 template <typename T>
 __global__ void wta_bwd_generic_kernel(const T* __restrict__ dy, const uint8_t* __restrict__ mask,
                                        T* __restrict__ dx, int64_t n_rows, int64_t d) {
@@ -515,10 +568,10 @@ __global__ void k_from_logits_kernel(const float* __restrict__ logits, int64_t n
   k_out[i] = static_cast<int32_t>(k);
 }
 
-template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST>
+template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST, bool GELU = false>
 int launch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, const int32_t* k_dev,
                  void* y, uint8_t* bitmask, int32_t* win, cudaStream_t st) {
-  auto kern = wta_fwd16_kernel<CH, BF, EXACT, WRITE_Y, HIST>;
+  auto kern = wta_fwd16_kernel<CH, BF, EXACT, WRITE_Y, HIST, GELU>;
   const size_t smem = HIST ? 256 * CH * 4 : 0;
   if (smem) TDX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
@@ -535,8 +588,17 @@ int launch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, const
 
 template <int CH, bool BF>
 int dispatch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, const int32_t* k_dev,
-                   int mode, void* y, uint8_t* bitmask, int32_t* win, cudaStream_t st) {
+                   int mode, void* y, uint8_t* bitmask, int32_t* win, cudaStream_t st, bool gelu = false) {
   const bool exact = mode == TAU_DXB_WTA_EXACT_K, wy = y != nullptr, h = win != nullptr;
+  if (gelu) {
+    if constexpr (BF) {
+      if (!exact && wy && h) return launch_fwd16<CH, true, false, true, true, true>(x, n_rows, row_stride, k, k_dev,
+                                                                                   y, bitmask, win, st);
+      if (!exact && wy && !h) return launch_fwd16<CH, true, false, true, false, true>(x, n_rows, row_stride, k,
+                                                                                     k_dev, y, bitmask, win, st);
+    }
+    return fail(TAU_DXB_ERR_UNSUPPORTED, "wta_fwd: GELU input needs bf16, threshold mode and y");
+  }
 #define TDX_WTA_CASE(E, W, H)                                                        \
   if (exact == E && wy == W && h == H)                                               \
     return launch_fwd16<CH, BF, E, W, H>(x, n_rows, row_stride, k, k_dev, y, bitmask, win, st);
@@ -551,14 +613,14 @@ int dispatch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, con
 template <bool BF>
 int dispatch_fwd16_width(int64_t d, const void* x, int64_t n_rows, int64_t row_stride, int k,
                          const int32_t* k_dev, int mode, void* y, uint8_t* bitmask, int32_t* win,
-                         cudaStream_t st) {
+                         cudaStream_t st, bool gelu = false) {
   switch (d / 256) {
-    case 3:  return dispatch_fwd16<3, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
-    case 4:  return dispatch_fwd16<4, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
-    case 6:  return dispatch_fwd16<6, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
-    case 8:  return dispatch_fwd16<8, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
-    case 12: return dispatch_fwd16<12, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
-    case 16: return dispatch_fwd16<16, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st);
+    case 3:  return dispatch_fwd16<3, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st, gelu);
+    case 4:  return dispatch_fwd16<4, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st, gelu);
+    case 6:  return dispatch_fwd16<6, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st, gelu);
+    case 8:  return dispatch_fwd16<8, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st, gelu);
+    case 12: return dispatch_fwd16<12, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st, gelu);
+    case 16: return dispatch_fwd16<16, BF>(x, n_rows, row_stride, k, k_dev, mode, y, bitmask, win, st, gelu);
     default: return 1;   // no fast kernel for this width
   }
 }
@@ -572,11 +634,20 @@ int wta_fwd_impl(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_
   if (n_rows == 0) return TAU_DXB_OK;
   TDX_CHECK_ARG(x && bitmask, "wta_fwd: x and bitmask are required");
   TDX_CHECK_ARG(row_stride >= d, "wta_fwd: row_stride (%lld) < d (%lld)", (long long)row_stride, (long long)d);
+  const bool gelu = (mode & TAU_DXB_WTA_GELU_INPUT) != 0;
+  mode &= ~TAU_DXB_WTA_GELU_INPUT;
   TDX_CHECK_ARG(mode == TAU_DXB_WTA_THRESHOLD || mode == TAU_DXB_WTA_EXACT_K, "wta_fwd: bad mode %d", mode);
   TDX_CHECK_ARG(dtype == TAU_DXB_F32 || dtype == TAU_DXB_BF16 || dtype == TAU_DXB_F16, "wta_fwd: bad dtype %d", dtype);
   const int kk = static_cast<int>(k < 1 ? 1 : (k > d ? d : k));
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (row_stride % 8 == 0) &&
                        (!y || reinterpret_cast<uintptr_t>(y) % 16 == 0);
+  if (gelu) {
+    TDX_CHECK_ARG(dtype == TAU_DXB_BF16 && aligned && d % 256 == 0 && y,
+                  "wta_fwd: GELU input needs bf16 rows of d a multiple of 256, 16-byte aligned, and y");
+    const int rc = dispatch_fwd16_width<true>(d, x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st, true);
+    if (rc == 1) return fail(TAU_DXB_ERR_UNSUPPORTED, "wta_fwd: no GELU-input kernel for d = %lld", (long long)d);
+    return rc;
+  }
   if (dtype != TAU_DXB_F32 && aligned && d % 256 == 0) {
     const int rc = dtype == TAU_DXB_BF16
         ? dispatch_fwd16_width<true>(d, x, n_rows, row_stride, kk, k_dev, mode, y, bitmask, win, st)
@@ -633,6 +704,23 @@ int wta_bwd_impl(const void* dy, int32_t dtype, const uint8_t* bitmask, int64_t 
   else
     wta_bwd_generic_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const __half*>(dy), bitmask, static_cast<__half*>(dx), n_rows, d);
   return check_launch("wta_bwd_generic_kernel");
+}
+
+int wta_bwd_gelu_impl(const void* dy, const void* x, const uint8_t* bitmask, int64_t n_rows, int64_t d, void* dx,
+                      cudaStream_t st) {
+  TDX_CHECK_ARG(n_rows >= 0 && d >= 1 && d % 8 == 0, "wta_bwd_gelu: need d a multiple of 8");
+  if (n_rows == 0) return TAU_DXB_OK;
+  TDX_CHECK_ARG(dy && x && bitmask && dx, "wta_bwd_gelu: dy, x, bitmask and dx are required");
+  TDX_CHECK_ARG(reinterpret_cast<uintptr_t>(dy) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(dx) % 16 == 0, "wta_bwd_gelu: dy, x and dx must be 16-byte aligned");
+  const int64_t n_bytes = n_rows * d / 8;
+  int64_t blocks = (n_bytes + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  wta_bwd_gelu_vec_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), bitmask,
+      static_cast<__nv_bfloat16*>(dx), n_bytes);
+  return check_launch("wta_bwd_gelu_vec_kernel");
 }
 
 int wta_k_from_logits_impl(const float* logits, int64_t n, int64_t d_ff, int32_t* k_out,

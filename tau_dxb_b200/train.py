@@ -103,6 +103,8 @@ def build_model(cfg: StepConfig, device, tau_init=None):
     model._tau_dxb_encoder_hook = contiguous_encoder_stream(model)
     LN.patch_layer_norms(model, bf16_out=single_gemm_norm)
     LIN.patch_linears(model)
+    if torch.device(device).type == "cuda":
+        SG.fuse_gelu_into_wta(model)        # encoder MLPs: GELU inside the WTA kernels
     model.train()
     return model
 

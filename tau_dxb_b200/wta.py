@@ -62,6 +62,21 @@ def wta_select(x: torch.Tensor, k, mode: int = THRESHOLD, write_y: bool = True,
     return y, bits
 
 
+def wta_backward_gelu(grad: torch.Tensor, x_pre: torch.Tensor, bits: torch.Tensor) -> torch.Tensor:
+    """dx = gelu'(x_pre) * (dy * keep) for a selection run on gelu(x_pre)
+    (wta_select(..., mode=THRESHOLD | C.WTA_GELU_INPUT)); bf16."""
+    _require_cuda(grad)
+    d = grad.shape[-1]
+    g = grad.contiguous()
+    xp = x_pre.contiguous()
+    dx = torch.empty_like(g)
+    n = g.numel() // d if d else 0
+    rc = C.lib().wta_bwd_gelu(g.data_ptr(), xp.data_ptr(), bits.data_ptr(), n, d, dx.data_ptr(),
+                              C.stream_ptr(g.device))
+    C.check("wta_bwd_gelu", rc)
+    return dx
+
+
 def wta_backward(grad: torch.Tensor, bits: torch.Tensor) -> torch.Tensor:
     """dx = dy * keep for a packed bitmask from wta_select."""
     _require_cuda(grad)
