@@ -96,23 +96,31 @@ ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma, cons
   }
 }
 
-template <int NCH, typename TD>
-__global__ void __launch_bounds__(kLnWarps * 32)
+// Backward CTA shape: 8 warps; 4 warps for rows of 768 and more, whose ~150
+// registers per thread would otherwise leave one 8-warp CTA per SM (4-warp
+// CTAs fit three: 12 warps of loads in flight instead of 8).
+constexpr int ln_bwd_warps(int nch) { return nch >= 6 ? 4 : 8; }
+constexpr int ln_bwd_ctas_per_sm(int nch) { return nch >= 6 ? 3 : 2; }
+
+template <int NCH, typename TD, int WARPS = ln_bwd_warps(NCH)>
+__global__ void __launch_bounds__(WARPS * 32)
 ln_bwd_kernel(const TD* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ mean_in,
               const float* __restrict__ rstd_in, const float* __restrict__ gamma, int64_t M,
               float* __restrict__ dx, float* __restrict__ part_dg, float* __restrict__ part_db) {
   constexpr int N = NCH * 128;
-  __shared__ float4 red[kLnWarps][NCH * 32];
+  __shared__ float4 red[WARPS][NCH * 32];
+  __shared__ float4 sg[NCH * 32];          // gamma, read per row
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * kLnWarps;
-  float4 g[NCH], adg[NCH], adb[NCH];
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * WARPS;
+  for (int i = threadIdx.x; i < NCH * 32; i += WARPS * 32) sg[i] = __ldg(reinterpret_cast<const float4*>(gamma) + i);
+  __syncthreads();
+  float4 adg[NCH], adb[NCH];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    g[c] = __ldg(reinterpret_cast<const float4*>(gamma) + c * 32 + lane);
     adg[c] = make_float4(0.f, 0.f, 0.f, 0.f);
     adb[c] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarps + warp; row < M; row += warps) {
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * WARPS + warp; row < M; row += warps) {
     const TD* dyr = dy + row * N;
     const float4* xr = reinterpret_cast<const float4*>(x + row * N);
     const float mean = __ldg(mean_in + row), rstd = __ldg(rstd_in + row);
@@ -123,7 +131,8 @@ ln_bwd_kernel(const TD* __restrict__ dy, const float* __restrict__ x, const floa
       d[c] = load4(dyr, c * 32 + lane);
       const float4 xv = __ldcs(xr + c * 32 + lane);
       xh[c] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd, (xv.w - mean) * rstd);
-      const float gx = g[c].x * d[c].x, gy = g[c].y * d[c].y, gz = g[c].z * d[c].z, gw = g[c].w * d[c].w;
+      const float4 gm = sg[c * 32 + lane];
+      const float gx = gm.x * d[c].x, gy = gm.y * d[c].y, gz = gm.z * d[c].z, gw = gm.w * d[c].w;
       s1 += (gx + gy) + (gz + gw);
       s2 = fmaf(gx, xh[c].x, fmaf(gy, xh[c].y, fmaf(gz, xh[c].z, fmaf(gw, xh[c].w, s2))));
       adg[c].x = fmaf(d[c].x, xh[c].x, adg[c].x);
@@ -140,10 +149,11 @@ ln_bwd_kernel(const TD* __restrict__ dy, const float* __restrict__ x, const floa
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       float4 o;
-      o.x = rstd * (g[c].x * d[c].x - m1 - xh[c].x * m2);
-      o.y = rstd * (g[c].y * d[c].y - m1 - xh[c].y * m2);
-      o.z = rstd * (g[c].z * d[c].z - m1 - xh[c].z * m2);
-      o.w = rstd * (g[c].w * d[c].w - m1 - xh[c].w * m2);
+      const float4 gm = sg[c * 32 + lane];
+      o.x = rstd * (gm.x * d[c].x - m1 - xh[c].x * m2);
+      o.y = rstd * (gm.y * d[c].y - m1 - xh[c].y * m2);
+      o.z = rstd * (gm.z * d[c].z - m1 - xh[c].z * m2);
+      o.w = rstd * (gm.w * d[c].w - m1 - xh[c].w * m2);
       dxr[c * 32 + lane] = o;
     }
   }
@@ -154,10 +164,10 @@ ln_bwd_kernel(const TD* __restrict__ dy, const float* __restrict__ x, const floa
 #pragma unroll
     for (int c = 0; c < NCH; ++c) red[warp][c * 32 + lane] = which ? adb[c] : adg[c];
     __syncthreads();
-    for (int col4 = threadIdx.x; col4 < NCH * 32; col4 += kLnWarps * 32) {
+    for (int col4 = threadIdx.x; col4 < NCH * 32; col4 += WARPS * 32) {
       float4 acc = red[0][col4];
 #pragma unroll
-      for (int w = 1; w < kLnWarps; ++w) {
+      for (int w = 1; w < WARPS; ++w) {
         const float4 v = red[w][col4];
         acc.x += v.x;
         acc.y += v.y;
@@ -171,21 +181,42 @@ ln_bwd_kernel(const TD* __restrict__ dy, const float* __restrict__ x, const floa
   }
 }
 
-// dgamma[c] = sum_b part_dg[b][c], dbeta likewise; one thread per column.
-__global__ void ln_bwd_reduce_kernel(const float* __restrict__ part_dg, const float* __restrict__ part_db,
-                                     int parts, int N, float* __restrict__ dgamma, float* __restrict__ dbeta) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= 2 * N) return;
+// dgamma[c] = sum_b part_dg[b][c], dbeta likewise. A CTA takes 32 columns of
+// the [2, parts, N] partials; its 8 warps each sum a contiguous range of the
+// partial rows (lane = column, coalesced), then warp 0 adds the 8 sums in
+// warp order: a fixed order, and 8 independent add chains per column instead
+// of one.
+constexpr int kLnRedWarps = 8;
+__global__ void __launch_bounds__(kLnRedWarps * 32)
+ln_bwd_reduce_kernel(const float* __restrict__ part_dg, const float* __restrict__ part_db, int parts, int N,
+                     float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  __shared__ float red[kLnRedWarps][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;          // over 2 N: dgamma columns, then dbeta
+  const bool ok = col < 2 * N;
   const float* src = col < N ? part_dg + col : part_db + (col - N);
+  const int per = (parts + kLnRedWarps - 1) / kLnRedWarps;
+  const int b0 = warp * per, b1 = b0 + per < parts ? b0 + per : parts;
   float acc = 0.f;
-  for (int b = 0; b < parts; ++b) acc += src[static_cast<int64_t>(b) * N];
-  if (col < N) dgamma[col] = acc;
-  else dbeta[col - N] = acc;
+  if (ok)
+    for (int b = b0; b < b1; ++b) acc += src[static_cast<int64_t>(b) * N];
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && ok) {
+    float t = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < kLnRedWarps; ++w) t += red[w][lane];
+    if (col < N) dgamma[col] = t;
+    else dbeta[col - N] = t;
+  }
 }
 
-int ln_parts(int64_t M) {
-  const int64_t want = (M + kLnWarps - 1) / kLnWarps;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 2;
+// backward CTAs (= partial rows): one wave of the CTAs that fit
+int ln_parts(int64_t M, int64_t N) {
+  const int nch = static_cast<int>(N / 128);
+  const int64_t warps = ln_bwd_warps(nch);
+  const int64_t want = (M + warps - 1) / warps;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * ln_bwd_ctas_per_sm(nch);
   return static_cast<int>(want < cap ? (want < 1 ? 1 : want) : cap);
 }
 
@@ -224,10 +255,10 @@ struct BwdLaunch {
   static int run(const void* dy, int dy_bf16, const float* x, const float* mean, const float* rstd, const float* g,
                  int64_t M, float* dx, float* pdg, float* pdb, int parts, cudaStream_t st) {
     if (dy_bf16)
-      ln_bwd_kernel<NCH, __nv_bfloat16><<<parts, kLnWarps * 32, 0, st>>>(
+      ln_bwd_kernel<NCH, __nv_bfloat16><<<parts, ln_bwd_warps(NCH) * 32, 0, st>>>(
           static_cast<const __nv_bfloat16*>(dy), x, mean, rstd, g, M, dx, pdg, pdb);
     else
-      ln_bwd_kernel<NCH, float><<<parts, kLnWarps * 32, 0, st>>>(static_cast<const float*>(dy), x, mean, rstd, g,
+      ln_bwd_kernel<NCH, float><<<parts, ln_bwd_warps(NCH) * 32, 0, st>>>(static_cast<const float*>(dy), x, mean, rstd, g,
                                                                  M, dx, pdg, pdb);
     return check_launch("ln_bwd_kernel");
   }
@@ -239,7 +270,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 size_t layer_norm_bwd_workspace(int64_t M, int64_t N) {
   if (M <= 0 || N <= 0) return 0;
-  return static_cast<size_t>(ln_parts(M)) * static_cast<size_t>(N) * 2 * sizeof(float);
+  return static_cast<size_t>(ln_parts(M, N)) * static_cast<size_t>(N) * 2 * sizeof(float);
 }
 
 int layer_norm_fwd_impl(const float* x, int64_t M, int64_t N, const float* gamma, const float* beta, float eps,
@@ -273,14 +304,14 @@ int layer_norm_bwd_impl(const void* dy, int32_t dy_dtype, const float* x, const 
   const size_t need = layer_norm_bwd_workspace(M, N);
   if (workspace_bytes < need)
     return fail(TAU_DXB_ERR_WORKSPACE, "layer norm: workspace of %zu bytes, need %zu", workspace_bytes, need);
-  const int parts = ln_parts(M);
+  const int parts = ln_parts(M, N);
   float* pdg = static_cast<float*>(workspace);
   float* pdb = pdg + static_cast<size_t>(parts) * N;
   int rc = dispatch_nch<BwdLaunch>(static_cast<int>(N), dy, static_cast<int>(dy_dtype == TAU_DXB_BF16), x, mean,
                                    rstd, gamma, M, dx, pdg, pdb, parts, st);
   if (rc) return rc;
-  const int threads = 256, blocks = static_cast<int>((2 * N + threads - 1) / threads);
-  ln_bwd_reduce_kernel<<<blocks, threads, 0, st>>>(pdg, pdb, parts, static_cast<int>(N), dgamma, dbeta);
+  const int blocks = static_cast<int>((2 * N + 31) / 32);
+  ln_bwd_reduce_kernel<<<blocks, kLnRedWarps * 32, 0, st>>>(pdg, pdb, parts, static_cast<int>(N), dgamma, dbeta);
   return check_launch("ln_bwd_reduce_kernel");
 }
 
