@@ -16,6 +16,8 @@
 //             dy is fp32 or bf16 (the gradient of a bf16 y). 12 (10) bytes per
 //             element plus 2 x 4 x d per CTA.
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace taudxb {
@@ -120,16 +122,46 @@ ln_bwd_kernel(const TD* __restrict__ dy, const float* __restrict__ x, const floa
     adg[c] = make_float4(0.f, 0.f, 0.f, 0.f);
     adb[c] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * WARPS + warp; row < M; row += warps) {
-    const TD* dyr = dy + row * N;
-    const float4* xr = reinterpret_cast<const float4*>(x + row * N);
-    const float mean = __ldg(mean_in + row), rstd = __ldg(rstd_in + row);
+  // the next row's dy and x are loaded while this one is processed
+  using DV = typename std::conditional<sizeof(TD) == 2, uint2, float4>::type;
+  auto ld_dy = [&](int64_t r, int c) -> DV { return __ldcs(reinterpret_cast<const DV*>(dy + r * N) + c * 32 + lane); };
+  auto to4 = [](DV v) -> float4 {
+    if constexpr (sizeof(TD) == 2)
+      return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
+                         __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+    else
+      return v;
+  };
+  int64_t row = static_cast<int64_t>(blockIdx.x) * WARPS + warp;
+  DV nd[NCH];
+  float4 nx[NCH];
+  if (row < M) {
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      nd[c] = ld_dy(row, c);
+      nx[c] = __ldcs(reinterpret_cast<const float4*>(x + row * N) + c * 32 + lane);
+    }
+  }
+  for (; row < M; row += warps) {
     float4 d[NCH], xh[NCH];
+    const float mean = __ldg(mean_in + row), rstd = __ldg(rstd_in + row);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      d[c] = to4(nd[c]);
+      xh[c] = nx[c];
+    }
+    const int64_t nrow = row + warps;
+    if (nrow < M) {
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        nd[c] = ld_dy(nrow, c);
+        nx[c] = __ldcs(reinterpret_cast<const float4*>(x + nrow * N) + c * 32 + lane);
+      }
+    }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
-      d[c] = load4(dyr, c * 32 + lane);
-      const float4 xv = __ldcs(xr + c * 32 + lane);
+      const float4 xv = xh[c];
       xh[c] = make_float4((xv.x - mean) * rstd, (xv.y - mean) * rstd, (xv.z - mean) * rstd, (xv.w - mean) * rstd);
       const float4 gm = sg[c * 32 + lane];
       const float gx = gm.x * d[c].x, gy = gm.y * d[c].y, gz = gm.z * d[c].z, gw = gm.w * d[c].w;
