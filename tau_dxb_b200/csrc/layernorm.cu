@@ -229,10 +229,19 @@ ln_bwd_reduce_kernel(const float* __restrict__ part_dg, const float* __restrict_
   const float* src = col < N ? part_dg + col : part_db + (col - N);
   const int per = (parts + kLnRedWarps - 1) / kLnRedWarps;
   const int b0 = warp * per, b1 = b0 + per < parts ? b0 + per : parts;
-  float acc = 0.f;
-  if (ok)
-    for (int b = b0; b < b1; ++b) acc += src[static_cast<int64_t>(b) * N];
-  red[warp][lane] = acc;
+  // four independent chains (loads in flight), added in a fixed order
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  if (ok) {
+    int b = b0;
+    for (; b + 3 < b1; b += 4) {
+      a0 += src[static_cast<int64_t>(b) * N];
+      a1 += src[static_cast<int64_t>(b + 1) * N];
+      a2 += src[static_cast<int64_t>(b + 2) * N];
+      a3 += src[static_cast<int64_t>(b + 3) * N];
+    }
+    for (; b < b1; ++b) a0 += src[static_cast<int64_t>(b) * N];
+  }
+  red[warp][lane] = (a0 + a1) + (a2 + a3);
   __syncthreads();
   if (warp == 0 && ok) {
     float t = red[0][lane];
@@ -247,7 +256,7 @@ ln_bwd_reduce_kernel(const float* __restrict__ part_dg, const float* __restrict_
 int ln_parts(int64_t M, int64_t N) {
   const int nch = static_cast<int>(N / 128);
   const int64_t warps = ln_bwd_warps(nch);
-  const int64_t want = (M + warps - 1) / warps;
+  const int64_t want = (M + 8 * warps - 1) / (8 * warps);     // at least 8 rows per warp
   const int64_t cap = static_cast<int64_t>(sm_count()) * ln_bwd_ctas_per_sm(nch);
   return static_cast<int>(want < cap ? (want < 1 ? 1 : want) : cap);
 }
