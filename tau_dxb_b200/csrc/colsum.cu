@@ -6,7 +6,7 @@
 // owns 8 columns of the tile (bf16) and walks rows r = split_lo + warp,
 // + 8, ...; the 8 warps add theirs through shared memory in a fixed order into
 // one fp32 partial row per split. Stage 2 adds the partial rows of each
-// column in split order. Same bits on every call.
+// column in a fixed order. Same bits on every call.
 
 #include "common.cuh"
 
@@ -76,13 +76,37 @@ colsum_partial_kernel(const T* __restrict__ x, int64_t M, int N, int64_t rows_pe
   }
 }
 
+// Stage 2: a CTA takes 32 columns; its 8 warps each sum a contiguous range of
+// the partial rows (lane = column, coalesced loads, four add chains), then
+// warp 0 adds the 8 sums in warp order -- a fixed order.
+constexpr int kCsRedWarps = 8;
 template <typename T>
-__global__ void colsum_final_kernel(const float* __restrict__ part, int splits, int N, T* __restrict__ out) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= N) return;
-  float s = 0.f;
-  for (int k = 0; k < splits; ++k) s += part[static_cast<int64_t>(k) * N + col];
-  out[col] = Elem<T>::from_f(s);
+__global__ void __launch_bounds__(kCsRedWarps * 32)
+colsum_final_kernel(const float* __restrict__ part, int splits, int N, T* __restrict__ out) {
+  __shared__ float red[kCsRedWarps][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  const int per = (splits + kCsRedWarps - 1) / kCsRedWarps;
+  const int k0 = warp * per, k1 = k0 + per < splits ? k0 + per : splits;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (col < N) {
+    int k = k0;
+    for (; k + 3 < k1; k += 4) {
+      s0 += part[static_cast<int64_t>(k) * N + col];
+      s1 += part[static_cast<int64_t>(k + 1) * N + col];
+      s2 += part[static_cast<int64_t>(k + 2) * N + col];
+      s3 += part[static_cast<int64_t>(k + 3) * N + col];
+    }
+    for (; k < k1; ++k) s0 += part[static_cast<int64_t>(k) * N + col];
+  }
+  red[warp][lane] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (warp == 0 && col < N) {
+    float t = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < kCsRedWarps; ++w) t += red[w][lane];
+    out[col] = Elem<T>::from_f(t);
+  }
 }
 
 void colsum_shape(int64_t M, int64_t N, int* splits, int64_t* rows_per_split) {
@@ -136,13 +160,13 @@ int column_sum_impl(const void* x, int32_t dtype, int64_t M, int64_t N, void* ou
                                                                   static_cast<int>(N), rps, part);
   int rc = check_launch("colsum_partial_kernel");
   if (rc) return rc;
-  const int threads = 256, blocks = static_cast<int>((N + threads - 1) / threads);
+  const int blocks = static_cast<int>((N + 31) / 32);
   if (out_dtype == TAU_DXB_BF16)
-    colsum_final_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(part, splits, static_cast<int>(N),
-                                                                   static_cast<__nv_bfloat16*>(out));
+    colsum_final_kernel<__nv_bfloat16><<<blocks, kCsRedWarps * 32, 0, st>>>(part, splits, static_cast<int>(N),
+                                                                             static_cast<__nv_bfloat16*>(out));
   else
-    colsum_final_kernel<float><<<blocks, threads, 0, st>>>(part, splits, static_cast<int>(N),
-                                                           static_cast<float*>(out));
+    colsum_final_kernel<float><<<blocks, kCsRedWarps * 32, 0, st>>>(part, splits, static_cast<int>(N),
+                                                                     static_cast<float*>(out));
   return check_launch("colsum_final_kernel");
 }
 
