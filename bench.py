@@ -773,6 +773,10 @@ def main():
                     help="only the WTA sub-benchmark (JSON of its results; for ncu captures)")
     ap.add_argument("--tau-star-only", action="store_true",
                     help="only the tau* solver sub-benchmark (JSON of its results; for ncu captures)")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the KV-cached decode sub-benchmark (JSON of its results; for ncu captures)")
+    ap.add_argument("--features-only", action="store_true",
+                    help="only the log-mel features sub-benchmark (JSON of its results; for ncu captures)")
     ap.add_argument("--train-only", action="store_true",
                     help="only the Whisper train-step sub-benchmark (JSON of its results; for ncu launch lists)")
     ap.add_argument("--torch-profile", default="",
@@ -811,12 +815,18 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return
-    if args.wta_only or args.tau_star_only:
+    if args.wta_only or args.tau_star_only or args.decode_only or args.features_only:
         device = torch.device("cuda", local_rank)
         torch.cuda.set_device(device)
         if rank == 0:
-            res = {"wta": wta_sub_bench(torch, device)} if args.wta_only else \
-                {"tau_star": tau_star_sub_bench(torch, device)}
+            if args.wta_only:
+                res = {"wta": wta_sub_bench(torch, device)}
+            elif args.tau_star_only:
+                res = {"tau_star": tau_star_sub_bench(torch, device)}
+            elif args.decode_only:
+                res = {"decode": decode_sub_bench(torch, device)}
+            else:
+                res = {"features": features_sub_bench(torch, device)}
             _emit(json.dumps(res), json_fd)
         if world > 1:
             dist.destroy_process_group()
