@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -495,7 +496,7 @@ def cpu_baseline_sample(reps=1):
                                      f"({t:.2f} s per sample, best of {reps})"}
 
 
-def e2e_bench(torch, r, c, device, world, n_steps, chunks=None):
+def e2e_bench(torch, r, c, device, world, n_steps, chunks=None, pipelined=True):
     """The headline step end to end through STauOpusAttentionFunction with
     pinned host buffers: every step copies Q, K, V, dO in and dQ, dK, dV,
     dlog_tau, dlog_alpha out, timed with CUDA events over n_steps steps (max
@@ -522,7 +523,7 @@ def e2e_bench(torch, r, c, device, world, n_steps, chunks=None):
     # dlog_tau / dlog_alpha are summed over the chunks on the device and read
     # back once per step.
     if chunks is None:
-        chunks = [2, 3, 3, 3, 3, 2] if B == 16 else [B]
+        chunks = ([8, 8] if pipelined else [2, 3, 3, 3, 3, 2]) if B == 16 else [B]
     assert sum(chunks) == B
     spans, o = [], 0
     for n in chunks:
@@ -565,6 +566,69 @@ def e2e_bench(torch, r, c, device, world, n_steps, chunks=None):
         cs.wait_stream(s_c)
         return dlt.cpu(), dla.cpu()
 
+    if pipelined:
+        # Successive steps overlap: step t+1's inputs stream in while step t
+        # computes and drains. Inputs land in two static device buffers (step
+        # t in slot t % 2, once step t - 2's kernels are done with it); the
+        # gradients read by the device->host stream are recorded on it; each
+        # step's dlog_tau / dlog_alpha go to pinned memory (two slots) and are
+        # read on the host two steps later.
+        dev_in = [[torch.empty_like(x, device=device) for x in hq] for _ in range(2)]
+        res_host = [torch.zeros(2, H).pin_memory() for _ in range(2)]
+        done_ev, res_ev, read_back, it = [None, None], [None, None], [], [0]
+
+        def e2e_step():
+            slot = it[0] % 2
+            it[0] += 1
+            if res_ev[slot] is not None:
+                res_ev[slot].synchronize()
+                read_back.append(float(res_host[slot][0, 0]))
+            ins = []
+            with torch.cuda.stream(s_in):
+                if done_ev[slot] is not None:
+                    s_in.wait_event(done_ev[slot])
+                for sl in spans:
+                    t = []
+                    for src, dst in zip(hq, dev_in[slot]):
+                        dst[sl].copy_(src[sl], non_blocking=True)
+                        t.append(dst[sl])
+                    ev = torch.cuda.Event()
+                    ev.record(s_in)
+                    ins.append((t, ev))
+            with torch.cuda.stream(s_c):
+                res = torch.zeros(2, H, device=device)
+            for sl, ((q, k, v, g), ev_in) in zip(spans, ins):
+                with torch.cuda.stream(s_c):
+                    s_c.wait_event(ev_in)
+                    q = q.detach().requires_grad_()
+                    k = k.detach().requires_grad_()
+                    v = v.detach().requires_grad_()
+                    ltp = lt.clone().requires_grad_()
+                    lap = la.clone().requires_grad_()
+                    out, _ = STauOpusAttentionFunction.apply(q, k, v, ltp, lap, c["sigma"], None, c["scale"])
+                    out.backward(g)
+                    res[0].add_(ltp.grad)
+                    res[1].add_(lap.grad)
+                    ev_c = torch.cuda.Event()
+                    ev_c.record(s_c)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev_c)
+                    for dst, src in zip(h_out, (q.grad, k.grad, v.grad)):
+                        src.record_stream(s_out)
+                        dst[sl].copy_(src, non_blocking=True)
+            with torch.cuda.stream(s_c):
+                ev = torch.cuda.Event()
+                ev.record(s_c)
+                done_ev[slot] = ev
+                res_host[slot].copy_(res, non_blocking=True)
+                ev2 = torch.cuda.Event()
+                ev2.record(s_c)
+                res_ev[slot] = ev2
+            return None
+
+        for st in (s_in, s_c, s_out):
+            st.wait_stream(cs)
+
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize()
@@ -574,10 +638,16 @@ def e2e_bench(torch, r, c, device, world, n_steps, chunks=None):
     s2 = torch.cuda.Event(enable_timing=True)
     e2 = torch.cuda.Event(enable_timing=True)
     s2.record(cs)
+    for st in (s_in, s_c, s_out):
+        st.wait_stream(cs)
     for _ in range(n_e2e):
         e2e_step()
+    for st in (s_in, s_c, s_out):
+        cs.wait_stream(st)
     e2.record(cs)
     torch.cuda.synchronize()
+    if pipelined:
+        assert read_back and all(math.isfinite(x) for x in read_back)
     te = torch.tensor([s2.elapsed_time(e2) / n_e2e], device=device)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
@@ -586,8 +656,10 @@ def e2e_bench(torch, r, c, device, world, n_steps, chunks=None):
             "d2h_bytes_per_step": int(d2h),
             "path": "STauOpusAttentionFunction.apply + backward, pinned host Q/K/V/dO in, "
                     "dQ/dK/dV/dlog_tau/dlog_alpha out",
-            "pipeline": f"batch chunks {chunks}; all H2D queued first, kernels and D2H per chunk, "
-                        "three streams"}
+            "pipeline": (f"batch chunks {chunks}; steps pipelined (step t+1's inputs stream in while step t "
+                         "computes and drains); H2D, kernels and D2H on three streams; each step's result is "
+                         "read on the host two steps later") if pipelined else
+                        f"batch chunks {chunks}; all H2D queued first, kernels and D2H per chunk, three streams"}
 
 
 def run_ours(args, rank, world, local_rank):
