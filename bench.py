@@ -428,7 +428,8 @@ def write_step_profile(torch, step, batch, path):
 
 def train_sub_bench(torch, device, world, rank, steps=10, warmup=3, profile_path=""):
     """Whisper-small tau-opus + WTA train step (batch 16 per GPU, bf16 autocast,
-    fp32 master weights, AdamW); DDP + NCCL all-reduce when world > 1.
+    fp32 master weights, AdamW); one NCCL all-reduce of all gradients per step
+    when world > 1.
     samples/s of the whole job, max-over-ranks CUDA-event time."""
     import torch.distributed as dist
     from tau_dxb_b200 import train as T
@@ -465,35 +466,52 @@ def train_sub_bench(torch, device, world, rank, steps=10, warmup=3, profile_path
            "model_tflop_per_step_per_gpu": round(flops / 1e12, 3),
            "mfu_of_sustained_bf16": round(flops / (ms * 1e-3) / (peak * 1e12), 4),
            "skipped_steps": step.skipped,
-           "parallelism": f"dp{world} (DDP, NCCL all-reduce of all gradients)" if world > 1 else "single GPU",
+           "parallelism": f"dp{world} (one NCCL all-reduce of the flat fp32 gradient buffer between the "
+                          "step's two CUDA graphs)" if world > 1 else "single GPU (two CUDA graphs)",
+           "parallelism_short": f"dp{world}",
            "data": "synthetic log-mel N(0,1) [16,80,3000], labels uniform over 51865, lengths U[64,448]"}
+    step.reset_graph()       # graphs released before the process group is destroyed
     del step
     torch.cuda.empty_cache()
     return out
 
 
-def cpu_baseline_sample(reps=1):
-    """The oracle (numpy) on a bounded sample: B=1, H=12, L=1500 encoder fwd+bwd."""
-    from oracle import stau_attention as OA
-    c = dict(ENC, B=1)
-    rng = np.random.default_rng(0)
-    Q, K, V, dO = (rng.standard_normal((1, 12, 1500, 64)).astype(np.float32) for _ in range(4))
-    lt = (rng.standard_normal(12) * 0.5).astype(np.float32)
-    la = np.zeros(12, np.float32)
+def host_threads():
+    """Host cores this process may run on (torchrun sets OMP_NUM_THREADS=1 for
+    its workers; the CPU arm sets its thread count from this instead)."""
     try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    except Exception:
-        cores = os.cpu_count() or 1
+        return len(os.sched_getaffinity(0))
+    except AttributeError:     # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def cpu_baseline_sample(reps=1):
+    """The reference's eager operator on the host cores, as its torch op
+    sequence (oracle/stau_attention_torch.py, pinned to the reference's golden
+    vectors): a bounded sample, B=1, H=12, L=1500 encoder fwd+bwd in fp32."""
+    import torch
+    from oracle import stau_attention_torch as OT
+    c = dict(ENC, B=1)
+    cores = host_threads()
+    old = torch.get_num_threads()
+    torch.set_num_threads(cores)
+    g = torch.Generator().manual_seed(0)
+    Q, K, V, dO = (torch.randn(1, 12, 1500, 64, generator=g) for _ in range(4))
+    lt = torch.randn(12, generator=g) * 0.5
+    la = torch.zeros(12)
     ts = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        OA.forward_backward(Q, K, V, lt, la, "softplus", dO, None, 0.125)
-        ts.append(time.perf_counter() - t0)
+    try:
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            OT.forward_backward(Q, K, V, lt, la, "softplus", dO, None, 0.125)
+            ts.append(time.perf_counter() - t0)
+    finally:
+        torch.set_num_threads(old)
     t = min(ts)
     return {"value": round(attn_flops(c) / t / 1e12, 5), "unit": "TFLOP/s", "cores": int(cores),
-            "kind": "port", "sample": "oracle fwd+bwd, encoder_self softplus B=1 H=12 L=1500 D=64 fp32 "
-                                     f"({t:.2f} s per sample, best of {reps})"}
+            "kind": "port", "impl": "torch CPU op sequence of the eager operator (echo/stau_opus_operator.py:66-166)",
+            "sample": "fwd+bwd, encoder_self softplus B=1 H=12 L=1500 D=64 fp32 "
+                      f"({t:.3f} s per sample, best of {reps})"}
 
 
 def e2e_bench(torch, r, c, device, world, n_steps, chunks=None, pipelined=True):
@@ -764,7 +782,7 @@ def run_ours(args, rank, world, local_rank):
         subs = {}
         for cfg in (DEC_SELF, DEC_CROSS):
             subs[cfg["name"]] = attn_sub_bench(torch, cfg, 7, device)
-        if args.long:
+        if not args.no_long:
             subs[LONG["name"]] = attn_sub_bench(torch, LONG, 8, device, iters=3, warm=1)
         result["attention_sites"] = subs
         result["decode"] = decode_sub_bench(torch, device)
@@ -780,6 +798,12 @@ def run_ours(args, rank, world, local_rank):
                             "in L2 when the kernel ends are not counted"}
     if rank == 0 and not args.no_cpu:
         result["cpu_baseline"] = cpu_baseline_sample(reps=8)
+    if rank == 0 and "train_step" in result:
+        # the multi-GPU headline of the train step, compact and last on the line
+        ts = result.pop("train_step")
+        result["train_step_detail"] = ts
+        result["train_step"] = {k: ts[k] for k in ("samples_per_s", "ms_per_step", "n_gpus", "global_batch",
+                                                   "mfu_of_sustained_bf16", "parallelism_short")}
     return result
 
 
@@ -792,12 +816,14 @@ def r_launches_per_step():
 
 def run_reference(args, rank, world):
     """The reference's CPU implementation of the path, timed on the host cores:
-    the oracle port (the reference is Python and is not installed here)."""
+    the torch op sequence of its eager operator (oracle/stau_attention_torch.py;
+    the reference itself is not present on the GPU machine), with every host
+    core this process may use, at every N."""
     if rank != 0:
         return None
     c = ENC
     samples = []
-    for _ in range(args.warmup):
+    for _ in range(min(args.warmup, 3)):
         cpu_baseline_sample()
     for _ in range(args.steps):
         samples.append(cpu_baseline_sample())
@@ -835,7 +861,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--quick", action="store_true", help="headline only (no sub-benchmarks)")
-    ap.add_argument("--long", action="store_true", help="add the L=6000 stress case")
+    ap.add_argument("--no-long", action="store_true", help="skip the L=6000 stress case")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-train", action="store_true", help="skip the Whisper train-step sub-benchmark")

@@ -82,9 +82,22 @@ TAU_DXB_API const char* tau_dxb_last_error(void);
 
 /* Device-side error word of the current device (0 = none): bit 1/2/4 = a
  * tensor-core kernel gave up waiting (TMA / MMA / softmax role) after its
- * time limit instead of hanging. Synchronises the device; reset != 0 clears
- * it. Returns -1 if it cannot be read. No reference counterpart (diagnostic). */
+ * time limit instead of hanging; TAU_DXB_DEVERR_SELFTEST = the wait of
+ * tau_dxb_selftest_wait_timeout gave up. Synchronises the device; reset != 0
+ * clears it. Returns -1 if it cannot be read. No reference counterpart
+ * (diagnostic). */
+#define TAU_DXB_DEVERR_SELFTEST 0x100
 TAU_DXB_API int tau_dxb_device_error(int32_t reset);
+
+/* Self-test of the bounded waits (no reference counterpart; diagnostic).
+ * Launches one CTA whose threads wait on an mbarrier phase that nothing
+ * completes, with a limit of `limit_ns` nanoseconds (0 < limit_ns <= 10 s)
+ * instead of the kernels' 2 s. The wait gives up, sets
+ * TAU_DXB_DEVERR_SELFTEST in the device error word and raises the CTA's abort
+ * flag; the CTA frees its tensor memory and returns. Synchronises `stream`.
+ * *status: bit 0 = a wait reported completion (a failure), bit 1 = the abort
+ * flag was raised (expected). No fault and no trap is involved. */
+TAU_DXB_API int tau_dxb_selftest_wait_timeout(uint64_t limit_ns, int32_t* status, void* stream);
 
 /*
  * tau-opus attention forward.
@@ -118,7 +131,8 @@ TAU_DXB_API int tau_attn_fwd(const void* q, const int64_t q_stride[4],
                  float* row_max, float* row_z, int32_t* row_argmax,
                  int32_t path, void* stream);
 
-/* Bytes of device workspace tau_attn_bwd needs for this problem. */
+/* Bytes of device workspace tau_attn_bwd needs for this problem (SIZE_MAX
+ * when the size does not fit a size_t: such a problem cannot run). */
 TAU_DXB_API size_t tau_attn_bwd_workspace_bytes(int64_t B, int64_t H, int64_t Lq, int64_t Lk,
                                     int64_t D);
 
@@ -166,10 +180,13 @@ TAU_DXB_API int tau_attn_bwd(const void* q, const int64_t q_stride[4],
  * Same arguments and results as tau_attn_bwd without the workspace; the scratch
  * lives in a fixed 16 MiB device array of the library (held on every GPU that
  * loads the library until exit). Problems needing more than 16 MiB of
- * workspace (tau_attn_bwd_workspace_bytes) return TAU_DXB_ERR_WORKSPACE. The
- * first call on a device resolves the array's address there; make it before
- * any stream capture. All calls on a device share the array: calls whose GPU
- * work overlaps race and must be serialised by the caller.
+ * workspace (tau_attn_bwd_workspace_bytes) return TAU_DXB_ERR_WORKSPACE. Each
+ * call resolves the array's address on the current device; the first call on
+ * a device also loads the library's device code there, so make it before any
+ * stream capture. All calls on a device share the array, which keeps the last
+ * call's contents (each call clears what must start at zero): calls whose GPU
+ * work overlaps race and must be serialised by the caller. The results are
+ * valid only if tau_dxb_device_error() reads 0 once the call's work is done.
  */
 TAU_DXB_API int tau_attn_bwd_noalloc(const void* q, const int64_t q_stride[4],
                  const void* k, const int64_t k_stride[4],

@@ -26,6 +26,7 @@ PATH_AUTO, PATH_PRECISE, PATH_TENSOR = 0, 1, 2
 WTA_THRESHOLD, WTA_EXACT_K = 0, 1
 WTA_GELU_INPUT = 0x100
 TAU_STAR_MAX_KEYS = 28672
+DEVERR_SELFTEST = 0x100
 
 _i64p = ctypes.POINTER(ctypes.c_int64)
 _vp = ctypes.c_void_p
@@ -38,6 +39,7 @@ SIGNATURES = {
     "tau_dxb_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "tau_dxb_last_error": (ctypes.c_char_p, []),
     "tau_dxb_device_error": (ctypes.c_int, [ctypes.c_int32]),
+    "tau_dxb_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_int32), _vp]),
     "tau_attn_fwd": (ctypes.c_int, [
         _vp, _i64p, _vp, _i64p, _vp, _i64p,           # q, k, v
         _i32, _i64, _i64, _i64, _i64, _i64,           # dtype, B, H, Lq, Lk, D

@@ -50,6 +50,7 @@ bool attn_tensor_supported(const AttnProblem& p);
 bool attn_tensor_bwd_supported(const AttnProblem& p);
 int read_device_error(int reset);
 int* device_error_word();   // device address of the kernels' error word
+int wait_selftest(uint64_t limit_ns, int32_t* status, cudaStream_t st);   // selftest.cu
 int attn_fwd_tensor(const AttnProblem& p, cudaStream_t st);
 int attn_bwd_tensor_main(const AttnProblem& p, cudaStream_t st);
 

@@ -216,13 +216,29 @@ size_t align_up(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
 }  // namespace
 
+// Products and sums that saturate at SIZE_MAX instead of wrapping, so that
+// no shape can make the required workspace look small.
+static size_t mul_sat(size_t a, size_t b) {
+  size_t r;
+  return __builtin_mul_overflow(a, b, &r) ? SIZE_MAX : r;
+}
+static size_t add_sat(size_t a, size_t b) {
+  size_t r;
+  return __builtin_add_overflow(a, b, &r) ? SIZE_MAX : r;
+}
+
 WorkspaceLayout workspace_layout(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D) {
   WorkspaceLayout w;
+  const size_t bh = mul_sat(static_cast<size_t>(B), static_cast<size_t>(H));
+  auto region = [&](int64_t L, int64_t d) {
+    const size_t bytes = mul_sat(mul_sat(mul_sat(bh, static_cast<size_t>(L)), static_cast<size_t>(d)), 4);
+    return bytes > SIZE_MAX - 255 ? SIZE_MAX : align_up(bytes);
+  };
   size_t o = 0;
-  w.dq = o;   o += align_up(static_cast<size_t>(B * H * Lq * D) * 4);
-  w.dk = o;   o += align_up(static_cast<size_t>(B * H * Lk * D) * 4);
-  w.drow = o; o += align_up(static_cast<size_t>(B * H * Lq) * 4);
-  w.rowf = o; o += align_up(static_cast<size_t>(B * H * Lq) * 4);
+  w.dq = o;   o = add_sat(o, region(Lq, D));
+  w.dk = o;   o = add_sat(o, region(Lk, D));
+  w.drow = o; o = add_sat(o, region(Lq, 1));
+  w.rowf = o; o = add_sat(o, region(Lq, 1));
   w.total = o;
   return w;
 }

@@ -216,6 +216,14 @@ int tau_attn_bwd(const void* q, const int64_t q_stride[4], const void* k, const 
 
 int tau_dxb_device_error(int32_t reset) { return read_device_error(reset); }
 
+int tau_dxb_selftest_wait_timeout(uint64_t limit_ns, int32_t* status, void* stream) {
+  g_last_error[0] = 0;
+  TDX_CHECK_ARG(status, "tau_dxb_selftest_wait_timeout: status is required");
+  TDX_CHECK_ARG(limit_ns > 0 && limit_ns <= 10000000000ull,
+                "tau_dxb_selftest_wait_timeout: limit_ns must be in (0, 10 s]");
+  return wait_selftest(limit_ns, status, static_cast<cudaStream_t>(stream));
+}
+
 int wta_fwd(const void* x, int32_t dtype, int64_t n_rows, int64_t d, int64_t row_stride, int64_t k,
             const int32_t* k_dev, int32_t mode, void* y, uint8_t* bitmask, int32_t* win_counts,
             void* stream) {

@@ -17,11 +17,12 @@
 //     contents: the regions that must start at zero are cleared on the stream
 //     by each call, and calls whose GPU work overlaps (two streams, or two
 //     host threads) race on the array -- serialise them;
-//   * the first call on a device resolves the array's device address with that
-//     device current (cudaGetSymbolAddress); make that first call before any
-//     stream capture begins.
-
-#include <mutex>
+//   * each call resolves the array's device address on the current device
+//     (cudaGetSymbolAddress; the first call on a device also loads the
+//     library's device code there, so make it before any stream capture);
+//   * the results are valid only if tau_dxb_device_error() reads 0 after the
+//     call's work is done: a tensor-core wait that gave up skips its stores,
+//     and the epilogue would then read what the array held from an earlier call.
 
 #include "attn.h"
 
@@ -34,25 +35,15 @@ constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;   // 16 MiB
 // kernels get the device address resolved by scratch_address().
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-void* g_scratch_ptr[kMaxDevices] = {nullptr};
-
-// Device address of the scratch array on the current device (set up once per device).
+// Device address of the scratch array on the current device. Resolved on
+// every call: a cached address would go stale if the caller reset the device
+// (cudaDeviceReset) and the module were loaded again elsewhere.
 int scratch_address(void** out) {
-  int dev = -1;
-  TDX_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kMaxDevices) return fail(TAU_DXB_ERR_UNSUPPORTED, "device index %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return fail(TAU_DXB_ERR_CUDA, "tau_attn_bwd_noalloc: cudaGetSymbolAddress failed: %s",
-                  cudaGetErrorString(e));
-    g_scratch_ptr[dev] = p;
-  }
-  *out = g_scratch_ptr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p)
+    return fail(TAU_DXB_ERR_CUDA, "tau_attn_bwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+  *out = p;
   return TAU_DXB_OK;
 }
 
@@ -70,6 +61,8 @@ extern "C" int tau_attn_bwd_noalloc(
     const float* row_max, const float* row_z, const int32_t* row_argmax, void* dq,
     const int64_t dq_stride[4], void* dk, const int64_t dk_stride[4], void* dv,
     const int64_t dv_stride[4], float* dtau, float* dalpha, int32_t path, void* stream) {
+  // tau_attn_bwd_workspace_bytes saturates instead of wrapping, so shapes too
+  // large for any workspace land here as well
   const size_t need = tau_attn_bwd_workspace_bytes(B, H, Lq, Lk, D);
   if (need > kNoAllocScratchBytes)
     return fail(TAU_DXB_ERR_WORKSPACE,

@@ -58,7 +58,7 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* err, int code) {
+                                          int* err, int code, uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -66,7 +66,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait_sleep(a, parity, 20000u)) return true;
     if ((it & 15u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         if (err) atomicOr(err, code);
         return false;

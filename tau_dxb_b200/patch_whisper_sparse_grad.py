@@ -35,7 +35,13 @@ import torch
 import torch.nn as nn
 
 from .wta import (THRESHOLD, SparseGradWTA_Function, WTA_Activation_Function,  # noqa: F401
-                  k_from_logits, wta_backward, wta_backward_gelu, wta_select)
+                  has_fused_kernels, k_from_logits, wta_backward, wta_backward_gelu, wta_fused_forward,
+                  wta_select)
+
+# The reference module's names for its fused WTA entry point and whether it
+# loaded (echo/patch_whisper_sparse_grad.py:26-31); here the CUDA kernels.
+_triton_wta_forward = wta_fused_forward
+_HAS_TRITON_WTA = has_fused_kernels()
 
 
 class _WTAFusedCounting(torch.autograd.Function):

@@ -259,17 +259,27 @@ class TrainStep:
         self.model = build_model(cfg, self.device, tau_init)
         self.world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
         self.net = PaddedHeadLoss(self.model).to(self.device)
-        if self.world > 1:
-            from torch.nn.parallel import DistributedDataParallel as DDP
-            self.net = DDP(self.net, device_ids=[self.device.index] if self.device.type == "cuda" else None,
-                           bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True,
-                           broadcast_buffers=False)
-        # one CUDA graph pair for the whole step: single GPU, no accumulation
-        # (LayerDrop draws on the host in every forward, which a graph would freeze)
+        # one CUDA graph pair for the whole step: no accumulation (LayerDrop
+        # draws on the host in every forward, which a graph would freeze)
         layerdrop = getattr(self.model.config, "encoder_layerdrop", 0.0) or getattr(self.model.config,
                                                                                 "decoder_layerdrop", 0.0)
-        self.graphed = bool(cuda_graph) and self.device.type == "cuda" and self.world == 1 \
-            and cfg.grad_accum == 1 and not layerdrop
+        self.graphed = bool(cuda_graph) and self.device.type == "cuda" and cfg.grad_accum == 1 \
+            and not layerdrop
+        # With more than one rank, the graphed step all-reduces one flat fp32
+        # gradient buffer between its two graphs (every .grad is a view of it);
+        # otherwise DistributedDataParallel reduces bucket by bucket.
+        self._flat = None
+        self._reduce_avg = False
+        if self.world > 1:
+            if self.graphed:
+                for t in list(self.net.parameters()) + list(self.net.buffers()):
+                    dist.broadcast(t.data, src=0)        # the replicas start identical, as DDP makes them
+                self._reduce_avg = dist.get_backend() == "nccl"
+            else:
+                from torch.nn.parallel import DistributedDataParallel as DDP
+                self.net = DDP(self.net, device_ids=[self.device.index] if self.device.type == "cuda" else None,
+                               bucket_cap_mb=bucket_mb, gradient_as_bucket_view=True,
+                               broadcast_buffers=False)
         self.opt = make_optimizer(self.model, cfg, capturable=self.graphed)
         self.sched = torch.optim.lr_scheduler.LambdaLR(
             self.opt, lr_lambda=lr_lambda(cfg.warmup_steps, cfg.t0_steps, cfg.t_mult))
@@ -399,6 +409,112 @@ class TrainStep:
         ev.record()
         self._pending = ev
 
+    # ---- data parallel over a flat gradient buffer (graphed, world > 1) ----
+
+    def _dp_local(self, mel, labels):
+        """Forward and backward into the flat gradient buffer (zeroed first);
+        the last slot of the buffer carries this rank's non-finite-loss flag
+        through the all-reduce."""
+        if self._flat is None:
+            self.opt.zero_grad(set_to_none=True)
+        else:
+            self._flat.zero_()
+        loss, _ = self.loss(mel, labels)
+        loss.backward()
+        if self._flat is None:
+            self._build_flat()
+        self._flat[-1:].copy_((~torch.isfinite(loss.detach())).float().reshape(1))
+        return loss.detach()
+
+    def _build_flat(self):
+        """After the first backward: one fp32 buffer holding every gradient the
+        step produced, each parameter's .grad becoming a view of it (the values
+        copied in). Parameters without a gradient keep .grad None, so AdamW
+        leaves them alone, as in the eager step."""
+        used = [p for p in self.model.parameters() if p.requires_grad and p.grad is not None]
+        n = sum(p.numel() for p in used)
+        flat = torch.zeros(n + 4, dtype=torch.float32, device=self.device)   # + the flag slot, 16-byte padded
+        off = 0
+        for p in used:
+            view = flat[off:off + p.numel()].view_as(p)
+            view.copy_(p.grad)
+            p.grad = view
+            off += p.numel()
+        self._flat = flat
+
+    def _dp_reduce(self):
+        """Average the gradients over the ranks (the flag slot becomes the
+        fraction of ranks with a non-finite loss). NCCL averages in the
+        collective; other backends sum, and the step scales afterwards."""
+        dist.all_reduce(self._flat, op=dist.ReduceOp.AVG if self._reduce_avg else dist.ReduceOp.SUM)
+
+    def _dp_finish(self):
+        """Scale (when the collective summed), the flag of the whole job as a
+        0-dim tensor, and clipping; returns the flag."""
+        if not self._reduce_avg:
+            self._flat.mul_(1.0 / self.world)
+        bad = (self._flat[-1] > 0).float()
+        torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.clip)
+        return bad
+
+    def _step_graphed_dp(self, mel, labels):
+        """The graphed step on each of several ranks: graph A = forward and
+        backward into the flat gradient buffer; then one all-reduce of the
+        buffer, issued between the replays (no collective inside a graph);
+        graph B = scaling, flag, clipping and the AdamW update. The previous
+        step is settled while A and the all-reduce run, before B changes the
+        weights."""
+        if self._gA is None and self._eager_calls < self.graph_warmup:
+            self._eager_calls += 1
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                loss = self._dp_local(mel, labels)
+                self._dp_reduce()
+                self.flush()
+                bad = self._dp_finish()
+                self.opt.found_inf = bad
+                self.opt.step()
+                self._post(bad)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            return loss
+        if self._gA is None:
+            self.flush()
+            torch.cuda.synchronize(self.device)
+            self._static = (mel.clone(), labels.clone())
+            gA, gB = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            tracker = SG._TRACKER
+            steps0 = dict(tracker.total_steps) if tracker is not None else {}
+            with torch.cuda.graph(gA):
+                self._sloss = self._dp_local(*self._static)
+            self._host_deltas = {k: v - steps0.get(k, 0) for k, v in tracker.total_steps.items()} \
+                if tracker is not None else {}
+            self._replays = 0
+            with torch.cuda.graph(gB, pool=gA.pool()):
+                self._sbad = self._dp_finish()
+                self.opt.found_inf = self._sbad
+                self.opt.step()
+            self._gA, self._gB = gA, gB
+        self._load_static(mel, labels)
+        self._gA.replay()
+        self._dp_reduce()
+        self.flush()
+        self._gB.replay()
+        self._post(self._sbad)
+        return self._sloss.clone()
+
+    def _load_static(self, mel, labels):
+        smel, slab = self._static
+        if mel.shape != smel.shape or labels.shape != slab.shape:
+            raise ValueError("TrainStep: batch shapes changed since the CUDA graph was captured "
+                             f"({tuple(smel.shape)}, {tuple(slab.shape)}); call reset_graph()")
+        smel.copy_(mel, non_blocking=True)
+        slab.copy_(labels, non_blocking=True)
+        if self._replays and SG._TRACKER is not None:
+            for k, d in self._host_deltas.items():
+                SG._TRACKER.total_steps[k] += d
+        self._replays += 1
+
     def _step_graphed(self, mel, labels):
         """The lagged step replayed from two CUDA graphs: A = forward, backward,
         clip and flag; B = the AdamW update (found_inf = the flag). The previous
@@ -406,6 +522,8 @@ class TrainStep:
         the weights before B changes them). The batch is copied into static
         buffers. The first graph_warmup calls are ordinary steps on a side
         stream; the next one captures both graphs, then replays them."""
+        if self.world > 1:
+            return self._step_graphed_dp(mel, labels)
         if self._gA is None and self._eager_calls < self.graph_warmup:
             self._eager_calls += 1
             side = torch.cuda.Stream(self.device)
@@ -439,16 +557,7 @@ class TrainStep:
             with torch.cuda.graph(gB, pool=gA.pool()):
                 self.opt.step()
             self._gA, self._gB = gA, gB
-        smel, slab = self._static
-        if mel.shape != smel.shape or labels.shape != slab.shape:
-            raise ValueError("TrainStep: batch shapes changed since the CUDA graph was captured "
-                             f"({tuple(smel.shape)}, {tuple(slab.shape)}); call reset_graph()")
-        smel.copy_(mel, non_blocking=True)
-        slab.copy_(labels, non_blocking=True)
-        if self._replays and SG._TRACKER is not None:
-            for k, d in self._host_deltas.items():
-                SG._TRACKER.total_steps[k] += d
-        self._replays += 1
+        self._load_static(mel, labels)
         self._gA.replay()
         self.flush()
         self._gB.replay()

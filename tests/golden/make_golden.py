@@ -6,8 +6,8 @@ echo/patch_whisper_sparse_grad.py and the LR lambda of
 echo/train_echo_opus1.py from it); the resulting .npz files are committed, so
 tests never need the reference at run time.
 
-    python tests/golden/make_golden.py [/path/to/reference]
-    TAU_DXB_GOLDEN_ONLY=lr_table python tests/golden/make_golden.py   # one table
+    python tests/golden/make_golden.py /path/to/reference
+    TAU_DXB_GOLDEN_ONLY=lr_table python tests/golden/make_golden.py /path/to/reference   # one table
 
 Every case is seeded; attention inputs and the reference's outputs are
 stored in fp32, WTA inputs/outputs as raw bf16 bit patterns (uint16) and
@@ -27,9 +27,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 def _ref_path(argv):
-    if len(argv) > 1:
-        return argv[1]
-    return os.environ.get("TAU_DXB_REFERENCE", "/root/reference")
+    if len(argv) < 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/reference-checkout")
+    return argv[1]
 
 
 def attn_cases():

@@ -96,3 +96,26 @@ def test_workspace_size_formula(C):
     n = lib.tau_attn_bwd_workspace_bytes(B, H, Lq, Lk, D)
     up = lambda v: (v + 255) // 256 * 256
     assert n == up(B * H * Lq * D * 4) + up(B * H * Lk * D * 4) + 2 * up(B * H * Lq * 4)
+
+
+def test_workspace_size_saturates_instead_of_wrapping(C):
+    """Shapes whose workspace does not fit a size_t report SIZE_MAX, so no
+    workspace (and not the no-allocation array) can look large enough."""
+    lib = C.lib()
+    size_max = 2 ** 64 - 1
+    assert lib.tau_attn_bwd_workspace_bytes(65535, 65535, (1 << 24) - 1, (1 << 24) - 1, 128) == size_max
+    assert lib.tau_attn_bwd_workspace_bytes(1 << 40, 1 << 40, 1, 1, 1) == size_max
+    s = (ctypes.c_int64 * 4)(0, 0, 0, 1)
+    p = ctypes.c_void_p(256)       # never dereferenced: the size check answers first
+    rc = lib.tau_attn_bwd_noalloc(p, s, p, s, p, s, p, s, p, s, C.BF16, 65535, 65535, (1 << 24) - 1,
+                                  (1 << 24) - 1, 128, p, p, 0, 0.125, None, 0, None, 0, p, p, p, p, s, p,
+                                  s, p, s, p, p, C.PATH_AUTO, None)
+    assert rc == C.ERR_WORKSPACE and "16 MiB" in C.last_error()
+
+
+def test_wait_selftest_validates_its_limit(C):
+    lib = C.lib()
+    st = ctypes.c_int32(0)
+    assert lib.tau_dxb_selftest_wait_timeout(0, ctypes.byref(st), None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_dxb_selftest_wait_timeout(11 * 10 ** 9, ctypes.byref(st), None) == C.ERR_INVALID_ARGUMENT
+    assert lib.tau_dxb_selftest_wait_timeout(10 ** 6, None, None) == C.ERR_INVALID_ARGUMENT

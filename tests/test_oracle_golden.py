@@ -35,6 +35,21 @@ def test_attention_oracle_matches_reference(path):
         assert rel_err(a, g[n]) < tol, (n, rel_err(a, g[n]))
 
 
+@pytest.mark.parametrize("path", ATTN_FILES, ids=lambda p: os.path.basename(p)[:-4])
+def test_torch_host_oracle_matches_reference(path):
+    """The torch restatement bench.py times as the reference's eager CPU path."""
+    from oracle import stau_attention_torch as OT
+    g = _load(path)
+    scale = float(g["scale"])
+    scale = None if np.isnan(scale) else scale
+    out, grads = OT.forward_backward(g["Q"], g["K"], g["V"], g["log_tau"], g["log_alpha"],
+                                     str(g["sigma"]), g["dO"], g.get("mask"), scale)
+    assert rel_err(out.numpy(), g["out"]) < 2e-6
+    for n, a in zip(["dQ", "dK", "dV", "dlog_tau", "dlog_alpha"], grads):
+        tol = 5e-5 if n.startswith("dlog") else 2e-5
+        assert rel_err(a.numpy(), g[n]) < tol, (n, rel_err(a.numpy(), g[n]))
+
+
 def test_attention_oracle_fp64_agrees():
     g = _load(os.path.join(GOLDEN, "attn_softplus_l65.npz"))
     out32, gr32, _ = OA.forward_backward(g["Q"], g["K"], g["V"], g["log_tau"], g["log_alpha"],
