@@ -493,6 +493,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         a2v[(e4 >> 1) + 1] = tc::fma2(make_float2(__uint_as_float(rr[e4 + 2]), __uint_as_float(rr[e4 + 3])),
                                       sa2x2, make_float2(mc4.z, mc4.w));
       }
+      // key rows past Lk (zero-filled by TMA, so s = 0 and a2 = -m alpha log2 e)
+      // take a2 = 0: their P is zeroed later, and a row max far below 0 would
+      // otherwise send the sigma polynomials out of range (inf * 0 = NaN)
+      if (!key_ok) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a2v[u] = make_float2(0.f, 0.f);
+      }
       const float m0 = tc::min3(a2v[0].x, a2v[0].y, a2v[1].x), m1 = tc::min3(a2v[1].y, a2v[2].x, a2v[2].y);
       const float m2 = tc::min3(a2v[3].x, a2v[3].y, a2v[4].x), m3 = tc::min3(a2v[4].y, a2v[5].x, a2v[5].y);
       const float m4 = tc::min3(a2v[6].x, a2v[6].y, a2v[7].x);
@@ -528,6 +535,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
               a2 = tc::fma2(make_float2(__uint_as_float(rr[e]), __uint_as_float(rr[e + 1])), sa2x2, mc);
               a2.x = fmaf(mv[e], al2, a2.x);
               a2.y = fmaf(mv[e + 1], al2, a2.y);
+              if constexpr (!kFull) {
+                if (!key_ok) a2 = make_float2(0.f, 0.f);   // key rows past Lk, as in chunk_a2
+              }
             } else {
               a2 = a2v[e >> 1];
             }

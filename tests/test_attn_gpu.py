@@ -276,6 +276,24 @@ def test_tensor_fwd_bwd_vs_oracle(A, sigma, causal, B, H, Lq, Lk):
     assert_close(mine, ref, TOL_BF16, f"tensor {sigma} {Lq}x{Lk}", zero_params=sigma == "relu")
 
 
+@pytest.mark.parametrize("sigma", ["sigmoid", "softplus"])
+@pytest.mark.parametrize("causal_fn", [False, True], ids=["mask_tensor", "causal_flag"])
+def test_tensor_causal_row_with_negative_max(A, sigma, causal_fn):
+    """Causal query row 0 sees key 0 only; with its score far below zero the
+    padded key rows of the last key tile (past Lk) must still contribute
+    nothing (they once turned dQ/dK row 0 and dlog_tau into NaN)."""
+    Q, K, V, lt, la, dO = make_inputs(2, 3, 200, 200, seed=17, dtype=torch.bfloat16)
+    K[:, :, 0] = (-0.6 * Q[:, :, 0].float()).to(torch.bfloat16)     # s00 = -0.6 |q0|^2 / 8, about -5
+    mask = torch.from_numpy(OA.causal_mask(200, 200))
+    assert_no_near_ties(Q, K, 0.125, mask)
+    mine = run_op(A, Q, K, V, lt, la, sigma, dO, None if causal_fn else mask, 0.125, path="tensor",
+                  causal_fn=causal_fn)
+    ref = oracle(Q, K, V, lt, la, sigma, dO, mask, 0.125)
+    for a in mine:
+        assert np.isfinite(a).all()
+    assert_close(mine, ref, TOL_BF16, f"negative row max {sigma}")
+
+
 def test_tensor_causal_flag_equals_mask(A):
     Q, K, V, lt, la, dO = make_inputs(2, 2, 190, 190, seed=5, dtype=torch.bfloat16)
     mask = torch.from_numpy(OA.causal_mask(190, 190))
