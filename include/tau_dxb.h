@@ -347,6 +347,19 @@ TAU_DXB_API int tau_column_sum(const void* x, int32_t dtype, int64_t M, int64_t 
                                void* stream);
 
 /*
+ * Soft-prune gradient mask: out = grad * keep along one axis.
+ * Replaces the gradient hooks of echo/patch_whisper_sparse_grad.py:167-194
+ * (fc1.weight rows, fc1.bias, fc2.weight columns) that prune_low_winners
+ * (echo/patch_whisper_sparse_grad.py:352-395) activates.
+ * grad, out: [rows, cols] row-major of `dtype` (may alias); keep: uint8 [rows]
+ * (axis 0) or [cols] (axis 1), nonzero = keep. The product is a multiply by
+ * 1.0 / 0.0 in the gradient's type, so a non-finite gradient under a 0 stays
+ * NaN, as in the reference.
+ */
+TAU_DXB_API int tau_grad_mask(const void* grad, int32_t dtype, int64_t rows, int64_t cols,
+                              const uint8_t* keep, int32_t axis, void* out, void* stream);
+
+/*
  * Cross-entropy over bf16 logits with fp32 math, the loss of
  * echo/train_echo_opus1.py:405-420 (F.cross_entropy of the LM-head logits,
  * labels == ignore_index not counted), without an fp32 copy of the logits.

@@ -85,6 +85,7 @@ SIGNATURES = {
                                           ctypes.c_size_t, _vp]),
     "tau_column_sum_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "tau_column_sum": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _i32, _vp, ctypes.c_size_t, _vp]),
+    "tau_grad_mask": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _i32, _vp, _vp]),
     "tau_cross_entropy_fwd": (ctypes.c_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
     "tau_cross_entropy_bwd": (ctypes.c_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp]),
 }

@@ -58,6 +58,7 @@ int tau_star_solve_impl(const float*, int64_t, int64_t, int64_t, int32_t, int32_
 int tau_star_analytic_impl(const float*, int64_t, int64_t, int64_t, int32_t, float*, cudaStream_t);
 size_t layer_norm_bwd_workspace(int64_t M, int64_t N);
 size_t column_sum_workspace(int64_t M, int64_t N);
+int grad_mask_impl(const void*, int32_t, int64_t, int64_t, const uint8_t*, int32_t, void*, cudaStream_t);
 int column_sum_impl(const void*, int32_t, int64_t, int64_t, void*, int32_t, void*, size_t, cudaStream_t);
 int cross_entropy_fwd_impl(const void*, int64_t, int64_t, const int64_t*, int64_t, float*, float*, cudaStream_t);
 int cross_entropy_bwd_impl(const void*, int64_t, int64_t, const int64_t*, int64_t, const float*, const float*, void*,
@@ -288,6 +289,12 @@ int tau_layer_norm_bwd(const void* dy, int32_t dy_dtype, const float* x, const f
   g_last_error[0] = 0;
   return layer_norm_bwd_impl(dy, dy_dtype, x, mean, rstd, gamma, M, d, dx, dgamma, dbeta, workspace,
                              workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int tau_grad_mask(const void* grad, int32_t dtype, int64_t rows, int64_t cols, const uint8_t* keep, int32_t axis,
+                  void* out, void* stream) {
+  g_last_error[0] = 0;
+  return grad_mask_impl(grad, dtype, rows, cols, keep, axis, out, static_cast<cudaStream_t>(stream));
 }
 
 size_t tau_column_sum_workspace_bytes(int64_t M, int64_t N) { return column_sum_workspace(M, N); }

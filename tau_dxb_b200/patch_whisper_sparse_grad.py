@@ -156,24 +156,46 @@ class LearnableKRatio(nn.Module):
         return f"logit_k={float(self.logit_k.detach()):.4f}"
 
 
+def masked_grad(grad: torch.Tensor, keep: torch.Tensor, axis: int) -> torch.Tensor:
+    """grad * keep along `axis` (0: rows, 1: columns) as the reference's hooks
+    compute it (echo/patch_whisper_sparse_grad.py:167-194). CUDA gradients run
+    on tau_grad_mask (one pass, the bool keep mask read as bytes); host
+    tensors use torch."""
+    if not grad.is_cuda:
+        m = keep.to(grad.device, grad.dtype)
+        return grad * (m.unsqueeze(-1) if axis == 0 and grad.dim() > 1 else m)
+    from . import _capi as C
+    g = grad.contiguous()
+    k = keep.to(device=g.device, dtype=torch.bool).contiguous()
+    rows = g.shape[0] if g.dim() > 1 else 1
+    cols = g.numel() // max(rows, 1) if g.dim() > 1 else g.numel()
+    if g.dim() == 1:       # a bias: one row, keep along its columns
+        axis = 1
+    out = torch.empty_like(g)
+    rc = C.lib().tau_grad_mask(g.data_ptr(), C.dtype_code(g.dtype), rows, cols, k.data_ptr(), axis,
+                               out.data_ptr(), C.stream_ptr(g.device))
+    C.check("tau_grad_mask", rc)
+    return out
+
+
 def _make_fc1_weight_grad_hook(module_name: str):
     def hook(grad):
         m = _GRAD_MASKS.get(module_name)
-        return grad if m is None else grad * m.to(grad.device, grad.dtype).unsqueeze(-1)
+        return grad if m is None else masked_grad(grad, m, 0)     # fc1.weight [d_ff, d_model]: rows
     return hook
 
 
 def _make_fc1_bias_grad_hook(module_name: str):
     def hook(grad):
         m = _GRAD_MASKS.get(module_name)
-        return grad if m is None else grad * m.to(grad.device, grad.dtype)
+        return grad if m is None else masked_grad(grad, m, 1)     # fc1.bias [d_ff]
     return hook
 
 
 def _make_fc2_weight_grad_hook(module_name: str):
     def hook(grad):
         m = _GRAD_MASKS.get(module_name)
-        return grad if m is None else grad * m.to(grad.device, grad.dtype).unsqueeze(0)
+        return grad if m is None else masked_grad(grad, m, 1)     # fc2.weight [d_model, d_ff]: columns
     return hook
 
 
