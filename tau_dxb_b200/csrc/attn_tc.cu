@@ -142,7 +142,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
   FwdBarriers* bars = reinterpret_cast<FwdBarriers*>(smem + kSmemBar);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * 2 * kBM;
-  const int nK = (p.Lk + kBN - 1) / kBN;
+  // Built-in causal mask (no mask tensor, Lq <= Lk): key tiles that every row
+  // of this CTA has masked are skipped. The reference gives each masked key
+  // the floor q = 1e-8; the row sums get that exactly (n_skip keys below), the
+  // output's share of it (1e-8 of the row weight per key) is dropped.
+  int nK = (p.Lk + kBN - 1) / kBN;
+  if (p.causal && !p.mask && p.Lq <= p.Lk) {
+    const int last_row = min(q0 + 2 * kBM, p.Lq) - 1;
+    const int lim = last_row + (p.Lk - p.Lq) + 1;      // keys >= lim are masked for every row here
+    nK = min(nK, max(1, (lim + kBN - 1) / kBN));
+  }
+  const int n_skip = max(0, p.Lk - nK * kBN);          // masked keys not visited
   volatile int* abort_flag = &bars->abort_flag;
 
   if (threadIdx.x == 0) {
@@ -545,7 +555,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_tc_kernel(const __gri
     xl[hc * kBM + r] = l0 + l1;
     xa[hc * kBM + r] = amax;
     tc::named_barrier_sync(1 + t, 256);
-    const float l = xl[hc * kBM + r] + xl[(hc ^ 1) * kBM + r];
+    const float l = xl[hc * kBM + r] + xl[(hc ^ 1) * kBM + r] +
+                    (n_skip ? static_cast<float>(n_skip) * tc::ex2(ylo) : 0.f);
     amax = min(amax, xa[(hc ^ 1) * kBM + r]);
     if (amax == INT_MAX) amax = 0;
     // epilogue: O / Z, this half's 32 output columns

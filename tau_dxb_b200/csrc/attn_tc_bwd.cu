@@ -149,7 +149,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
   float* stats = reinterpret_cast<float*>(smem + kOffStats);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y, k0 = blockIdx.x * kT;
-  const int nQ = (p.Lq + kT - 1) / kT;
+  // Built-in causal mask (no mask tensor): query tiles whose every row sees
+  // none of this CTA's keys are skipped. Their masked scores carry only the
+  // reference's floor q = 1e-8 per key, so their share of every gradient is
+  // below 1e-8 of the row's weight (under the bf16 rounding of P).
+  // (Lq <= Lk only: with Lq > Lk the first rows see no key at all, and the
+  // reference gives such rows uniform weights that are not negligible.)
+  const bool causal_only = p.causal && !p.mask && p.Lq <= p.Lk;
+  int qt0 = 0;                   // first query tile with an unmasked (query, key) pair here
+  if (causal_only) {
+    const int lim = k0 - (p.Lk - p.Lq);      // rows >= lim see key k0
+    qt0 = lim > 0 ? lim / kT : 0;
+  }
+  const int nQ = (p.Lq + kT - 1) / kT - qt0;   // tiles streamed: qt0 .. qt0 + nQ - 1
   const int64_t bh = static_cast<int64_t>(b) * p.H + h;
   volatile int* abort_flag = &bars->abort_flag;
 
@@ -200,8 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         if (i >= kQStages && !tc::mbar_wait(&bars->qd_empty[s], ph ^ 1, abort_flag, p.err, kErrTimeoutTma))
           break;
         tc::mbar_arrive_expect_tx(&bars->qd_full[s], 2 * kTile);
-        tc::tma_load_4d(smem + kOffQ + s * kTile, &p.tq, &bars->qd_full[s], 0, i * kT, h, b);
-        tc::tma_load_4d(smem + kOffDO + s * kTile, &p.tdo, &bars->qd_full[s], 0, i * kT, h, b);
+        tc::tma_load_4d(smem + kOffQ + s * kTile, &p.tq, &bars->qd_full[s], 0, (qt0 + i) * kT, h, b);
+        tc::tma_load_4d(smem + kOffDO + s * kTile, &p.tdo, &bars->qd_full[s], 0, (qt0 + i) * kT, h, b);
         issued = i + 1;
         if (++s == kQStages) { s = 0; ph ^= 1; }
       }
@@ -296,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       float m4[4], z4[4], d4[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int q = i * kT + lane + 32 * u;
+        const int q = (qt0 + i) * kT + lane + 32 * u;
         const int64_t ri = bh * p.Lq + (q < p.Lq ? q : 0);
         m4[u] = p.row_max[ri];
         z4[u] = p.row_z[ri];
@@ -305,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int r = lane + 32 * u;
-        const bool q_ok = i * kT + r < p.Lq;
+        const bool q_ok = (qt0 + i) * kT + r < p.Lq;
         st[r] = q_ok ? -m4[u] * al2 : 0.f;
         st[kT + r] = q_ok ? 1.f / z4[u] : 0.f;
         st[2 * kT + r] = q_ok ? d4[u] : 0.f;
@@ -355,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         tc::fence_async_smem();
         tc::named_barrier_sync(1, 128);
         if (threadIdx.x == 128) {
-          tc::tma_reduce_add_3d(&p.tdq, stage, 32 * half, j * kT, static_cast<int>(bh));
+          tc::tma_reduce_add_3d(&p.tdq, stage, 32 * half, (qt0 + j) * kT, static_cast<int>(bh));
           tc::bulk_commit_group();
         }
       }
@@ -391,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
           v[u] = keep + __shfl_xor_sync(0xffffffffu, send, lvl);
         }
       }
-      const int q = j * kT + (r >> 6) * 64 + c8 * 8 + kp;
+      const int q = (qt0 + j) * kT + (r >> 6) * 64 + c8 * 8 + kp;
       if (q < p.Lq) atomicAdd(p.ws_rowf + bh * p.Lq + q, v[0] * ta);
     }
     if (threadIdx.x == 128) tc::bulk_wait_group0();
@@ -466,7 +478,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       }
     }
     const bool tile_full = k0 + kT <= p.Lk;
-    const bool has_mask = p.mask != nullptr || p.causal;
     float2 acc_tau = make_float2(0.f, 0.f), acc_alpha = make_float2(0.f, 0.f);
     int qs = 0, qph = 0;             // stage and phase of tile i in the Q / dO / statistics ring
     // Clean chunks: where every x = alpha (s - m) of the chunk is above
@@ -515,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
       if constexpr (kMasked) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const int q = i * kT + col0 + e;
+          const int q = (qt0 + i) * kT + col0 + e;
           mv[e] = (key_ok && q < p.Lq) ? bwd_mask_value(p, b, h, q, key) : 0.f;
         }
       }
@@ -594,7 +605,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         // branch-free bodies (mask / partial key tile decided per chunk) so the
         // scheduler can interleave the eight column pairs
         float2 a2v[8];
-        if (has_mask) {
+        // with the built-in causal mask only, a chunk none of whose (key,
+        // query) pairs of this warp is masked takes the unmasked path
+        const bool masked = p.mask != nullptr ||
+                            (p.causal && (!causal_only ||
+                                          k0 + ((warp & 3) << 5) + 31 > (qt0 + i) * kT + col0 + (p.Lk - p.Lq)));
+        if (masked) {
           if (tile_full) chunk_math(BoolC<true>{}, BoolC<true>{}, BoolC<false>{}, rr, i, col0, a2v, pp, pf);
           else chunk_math(BoolC<true>{}, BoolC<false>{}, BoolC<false>{}, rr, i, col0, a2v, pp, pf);
         } else if (chunk_a2(rr, col0, a2v)) {

@@ -119,9 +119,11 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
 // compare per two elements (set.ge.u32.{bf16x2,f16x2} gives 0xFFFF per true
 // half) and one subtraction into a register accumulator, then one warp
 // reduction. The search starts at the threshold of the row this warp did
-// before (rows of one activation tensor are alike): it gallops away from it
-// until the answer is bracketed, then bisects; the first row of a warp
-// bisects the whole range.
+// before (rows of one activation tensor are alike) -- for a warp's first row,
+// the threshold its slot ended on in the previous launch -- probes once at the
+// distance the count there suggests (the count difference times the keys per
+// unit of count seen on earlier rows), gallops away from the bracket edge that
+// probe set, then bisects; without a start it bisects the whole range.
 //
 // The compares are float compares, as in the reference: +0 == -0. The search
 // counts NaN as larger than everything (set.geu), as torch.topk / kthvalue
@@ -193,6 +195,17 @@ __device__ __forceinline__ uint32_t mask_byte(uint32_t m0, uint32_t m1, uint32_t
 constexpr int kFastWarps = 4;                    // rows in flight per block
 constexpr uint32_t kGallopMax = 64;
 
+// Search warm start across launches: the threshold key each warp of the fast
+// kernel ended on, and its estimate of keys per unit of count near the
+// threshold, kept per (block, warp) slot. The next launch starts each warp's
+// first row from its slot instead of bisecting the whole key range. A slot
+// only says where a search begins -- the bracket search below is exact from
+// any start -- so launches that race on a slot (two streams) still give exact
+// results. The tag in bits 16+ keeps bf16 and f16 key spaces apart.
+constexpr int kHintSlots = 8192;
+__device__ uint32_t g_wta_hint_key[kHintSlots];
+__device__ float g_wta_hint_ipc[kHintSlots];
+
 template <bool B> struct BoolC { static constexpr bool value = B; };
 
 // GELU (erf form) as PyTorch's CUDA kernels evaluate it for bf16 tensors: fp32
@@ -252,9 +265,26 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
   }
   // warp-uniform search state: the previous row's threshold key and how far
   // it moved from the row before; galloping pays while that distance is small
-  // (about 2 log2(distance) + 2 probes against 16 for a full bisection)
+  // (about 2 log2(distance) + 2 probes against 16 for a full bisection).
+  // ipc: keys per unit of count near the threshold (from the rows searched so
+  // far), which turns the first probe's count into a jump estimate.
+  constexpr uint32_t kTag = BF ? 0x10000u : 0x20000u;
+  const int slot = blockIdx.x * kFastWarps + warp;
   bool have_prev = false;
   uint32_t t_prev = 0, dist_prev = 0;
+  float ipc = 0.25f;
+  if (slot < kHintSlots) {
+    const uint32_t h = g_wta_hint_key[slot];
+    if ((h & 0xFFFF0000u) == kTag) {
+      const uint32_t hk = h & 0xFFFFu;
+      if (hk >= kNeg && hk <= kPos) {
+        have_prev = true;
+        t_prev = hk;
+        const float hi_pc = g_wta_hint_ipc[slot];
+        if (hi_pc > 0.f && hi_pc < 64.f) ipc = hi_pc;
+      }
+    }
+  }
   for (; row < n_rows; row += stride_rows) {
     uint4 w[CH];
 #pragma unroll
@@ -298,10 +328,36 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
     // sentinel hi = kPos + 1 ("above +inf"); count(kNeg) = d >= k.
     uint32_t lo = kNeg, hi = kPos + 1;
     const bool gallop = have_prev && dist_prev <= kGallopMax;
+    int c0 = 0;
+    uint32_t t_start = t_prev;
     if (gallop) {
-      const int c = count_ge(t_prev, BoolC<true>{});
-      if (c >= k) {
+      // count at the previous threshold; then one probe at the estimate
+      // t_prev +- |c0 - k| * ipc, which usually lands on or next to the
+      // answer; then gallop from the bracket edge it set, and bisect
+      c0 = count_ge(t_prev, BoolC<true>{});
+      const float dest = fminf(static_cast<float>(abs(c0 - k)) * ipc + 0.5f, 256.f);
+      const uint32_t d = max(1u, static_cast<uint32_t>(dest));
+      bool up;
+      if (c0 >= k) {
         lo = t_prev;
+        const uint32_t p = lo + d < hi ? lo + d : hi - 1;
+        up = true;
+        if (p > lo) {
+          if (count_ge(p, BoolC<true>{}) >= k) lo = p;
+          else { hi = p; up = false; }
+        }
+      } else {
+        hi = t_prev;
+        const uint32_t p = hi - kNeg > d ? hi - d : kNeg;
+        up = false;
+        if (p < hi && p > kNeg) {
+          if (count_ge(p, BoolC<true>{}) >= k) { lo = p; up = true; }
+          else hi = p;
+        } else {
+          lo = kNeg;
+        }
+      }
+      if (up) {            // the answer is at lo or above: walk up
         for (uint32_t step = 1; lo + step < hi; step <<= 1) {
           const uint32_t p = lo + step;
           if (count_ge(p, BoolC<true>{}) >= k) {
@@ -311,9 +367,8 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
             break;
           }
         }
-      } else {
-        hi = t_prev;
-        for (uint32_t step = 1; hi - kNeg > step; step <<= 1) {
+      } else {             // the answer is below hi: walk down
+        for (uint32_t step = 1; hi - lo > step; step <<= 1) {
           const uint32_t p = hi - step;
           if (count_ge(p, BoolC<true>{}) >= k) {
             lo = p;
@@ -340,6 +395,11 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
       c_gt = count_ge(t + 1, BoolC<false>{});
     }
     dist_prev = have_prev ? (t > t_prev ? t - t_prev : t_prev - t) : 0u;
+    if (gallop && t != t_start && c0 != k) {
+      // keys per unit of count between the previous threshold and this one
+      const float r = static_cast<float>(dist_prev) / static_cast<float>(abs(c0 - k));
+      ipc = 0.5f * (ipc + fminf(r, 64.f));
+    }
     t_prev = t;
     have_prev = true;
     const uint32_t tb = key_to_bits16(t);
@@ -390,6 +450,10 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
           if ((bits >> e) & 1u) atomicAdd(&shist[col0 + e], 1);
       }
     }
+  }
+  if (have_prev && lane == 0 && slot < kHintSlots) {     // warm start for the next launch
+    g_wta_hint_key[slot] = kTag | t_prev;
+    g_wta_hint_ipc[slot] = ipc;
   }
   if (HIST) {
     __syncthreads();
