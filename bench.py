@@ -386,6 +386,87 @@ def wta_sub_bench(torch, device, iters=20, warm=3):
     return res
 
 
+def capture_run(torch, device, family, iters=2, warm=3):
+    """One kernel family at its workload size, alone: warm-up calls, then
+    `iters` timed calls (CUDA events). For ncu captures of single kernels;
+    prints what it timed."""
+    from tau_dxb_b200 import _capi as C
+    cs = torch.cuda.current_stream()
+    g = torch.Generator(device=device).manual_seed(77)
+    res = {}
+
+    def timed(name, fn):
+        for _ in range(warm):
+            fn()
+        res[name] = round(time_events(torch, fn, iters, cs), 4)
+
+    if family == "attn_sites":            # decoder_self (causal) and decoder_cross, B=16
+        for cfg in (DEC_SELF, DEC_CROSS):
+            r = AttnRunner(torch, cfg, 7, device)
+            timed(cfg["name"] + "_fwd_ms", lambda: r.fwd(cs.cuda_stream))
+            timed(cfg["name"] + "_bwd_ms", lambda: r.bwd(cs.cuda_stream))
+            del r
+    elif family == "attn_precise":        # fp32 precise path, encoder_self B=1
+        from tau_dxb_b200 import attention as A
+        c = dict(ENC, B=1)
+        q, k, v, do, lt, la = make_attn_inputs(torch, c, 5, device)
+        q, k, v, do = (t.float().requires_grad_(t is not do) for t in (q, k, v, do))
+        lt, la = lt.requires_grad_(), la.requires_grad_()
+
+        def step():
+            with A.attention_path("precise"):
+                out, _ = A.STauOpusAttentionFunction.apply(q, k, v, lt, la, "softplus", None, 0.125)
+                out.backward(do)
+        timed("precise_fwd_bwd_ms", step)
+    elif family == "wta_extra":           # generic fp32 select, GELU-fused backward, decoder forward
+        from tau_dxb_b200 import wta as W
+        xf = torch.nn.functional.gelu(torch.randn(24000, 3072, device=device, generator=g))
+        timed("generic_f32_fwd_ms", lambda: W.wta_select(xf, 306, W.THRESHOLD))
+        xb = xf.to(torch.bfloat16)
+        _, bits = W.wta_select(xb, 306, W.THRESHOLD)
+        dy = torch.randn(24000, 3072, device=device, generator=g).to(torch.bfloat16)
+        timed("bwd_gelu_ms", lambda: W.wta_backward_gelu(dy, xb, bits))
+        xd = xb[:7168].contiguous()
+        timed("decoder_mask_fwd_ms", lambda: W.wta_select(xd, 306, W.THRESHOLD, write_y=False))
+    elif family == "train_kernels":       # layer norm, column sums, cross-entropy, prune mask
+        from tau_dxb_b200 import layernorm as LN
+        from tau_dxb_b200 import linear as LIN
+        from tau_dxb_b200 import patch_whisper_sparse_grad as SG
+        x = torch.randn(24000, 768, device=device, generator=g).requires_grad_()
+        w = torch.ones(768, device=device, requires_grad=True)
+        b = torch.zeros(768, device=device, requires_grad=True)
+        dyn = torch.randn(24000, 768, device=device, generator=g).to(torch.bfloat16)
+
+        def ln():
+            y = LN.fused_layer_norm(x, w, b, 1e-5, out_bf16=True)
+            y.backward(dyn)
+        timed("layer_norm_fwd_bwd_ms", ln)
+        gb = torch.randn(24000, 3072, device=device, generator=g).to(torch.bfloat16)
+        timed("column_sum_ms", lambda: LIN.column_sum(gb))
+        logits = torch.randn(7168, 51904, device=device, generator=g).to(torch.bfloat16).requires_grad_()
+        labels = torch.randint(0, 51865, (7168,), device=device, generator=g)
+
+        def xent():
+            LIN.cross_entropy(logits, labels).backward()
+        timed("cross_entropy_fwd_bwd_ms", xent)
+        gw = torch.randn(3072, 768, device=device, generator=g)
+        keep = torch.rand(3072, device=device, generator=g) > 0.3
+        timed("grad_mask_ms", lambda: SG.masked_grad(gw, keep, 0))
+    elif family == "fixed":               # fixed-tau weights, cross-attention shape, fp32 scores
+        from tau_dxb_b200 import patch_whisper_stau as P
+        sc = (torch.randn(16, 12, 448, 1500, device=device, generator=g) * 2).requires_grad_()
+        tau = (1 + torch.rand(12, device=device, generator=g)).view(1, 12, 1, 1)
+        dA = torch.randn(16, 12, 448, 1500, device=device, generator=g)
+
+        def fx():
+            P.STauOpusMaxStableFn.apply(sc, tau, "softplus").backward(dA)
+        timed("fixed_fwd_bwd_ms", fx)
+    else:
+        raise SystemExit(f"unknown --capture family {family}")
+    torch.cuda.synchronize()
+    return {"capture": family, **res}
+
+
 def write_step_profile(torch, step, batch, path):
     """One eager train step under torch.profiler: ops by self device time,
     and for every copy kernel over 20 us the chain of ops that launched it."""
@@ -877,6 +958,9 @@ def main():
                     help="only the log-mel features sub-benchmark (JSON of its results; for ncu captures)")
     ap.add_argument("--train-only", action="store_true",
                     help="only the Whisper train-step sub-benchmark (JSON of its results; for ncu launch lists)")
+    ap.add_argument("--capture", default="",
+                    help="run one kernel family alone for an ncu capture: attn_sites, attn_precise, wta_extra, "
+                         "train_kernels, fixed")
     ap.add_argument("--torch-profile", default="",
                     help="with --train-only: profile one more step with torch.profiler and write its top "
                          "device-time ops and the callers of its copy kernels to this file")
@@ -910,6 +994,14 @@ def main():
                              profile_path=args.torch_profile)
         if rank == 0:
             _emit(json.dumps({"train_step": ts}), json_fd)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    if args.capture:
+        device = torch.device("cuda", local_rank)
+        torch.cuda.set_device(device)
+        if rank == 0:
+            _emit(json.dumps(capture_run(torch, device, args.capture)), json_fd)
         if world > 1:
             dist.destroy_process_group()
         return

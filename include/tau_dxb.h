@@ -50,6 +50,7 @@ extern "C" {
 #define TAU_DXB_SIGMA_SIGMOID  1
 #define TAU_DXB_SIGMA_EXP      2
 #define TAU_DXB_SIGMA_RELU     3
+#define TAU_DXB_SIGMA_TANH_SHIFT 4  /* tanh(x) + 1; fixed-tau weights (tau_opus_fixed_*) only */
 
 /* ---- longest score row tau_star_solve accepts --------------------------- */
 #define TAU_DXB_TAU_STAR_MAX_KEYS 28672
@@ -345,6 +346,31 @@ TAU_DXB_API size_t tau_column_sum_workspace_bytes(int64_t M, int64_t N);
 TAU_DXB_API int tau_column_sum(const void* x, int32_t dtype, int64_t M, int64_t N, void* out,
                                int32_t out_dtype, void* workspace, size_t workspace_bytes,
                                void* stream);
+
+/*
+ * Fixed-tau attention weights from materialised scores: the forward of
+ * STauOpusMaxStableFn (echo/patch_whisper_stau.py:74-87), the operator of the
+ * fixed-tau patch (apply_fixed_stau, echo/patch_whisper_stau.py:279-322).
+ * scores: fp32 rows of length L, `row_stride` elements apart; attn: fp32
+ * [rows, L] contiguous. Per row: x = s - max(s), q = max(sigma(x), 1e-8)^tau,
+ * attn = q / max(sum q, 1e-8). tau: fp32 device array of n_tau values; row r
+ * uses tau[(r / rows_per_tau) % n_tau] (n_tau = H and rows_per_tau = Lq for
+ * [B, H, Lq, Lk] scores and a per-head tau; n_tau = 1 for one tau).
+ * sigma: TAU_DXB_SIGMA_SOFTPLUS .. TAU_DXB_SIGMA_TANH_SHIFT.
+ */
+TAU_DXB_API int tau_opus_fixed_fwd(const float* scores, int64_t rows, int64_t L, int64_t row_stride,
+                                   const float* tau, int64_t n_tau, int64_t rows_per_tau,
+                                   int32_t sigma_id, float* attn, void* stream);
+
+/*
+ * Its backward (echo/patch_whisper_stau.py:89-112): grad_scores from the
+ * upstream gradient of attn (fp32 [rows, L] contiguous), the same scores, tau
+ * and sigma; grad_scores is fp32 [rows, L] contiguous.
+ */
+TAU_DXB_API int tau_opus_fixed_bwd(const float* scores, const float* grad_attn, int64_t rows, int64_t L,
+                                   int64_t row_stride, const float* tau, int64_t n_tau,
+                                   int64_t rows_per_tau, int32_t sigma_id, float* grad_scores,
+                                   void* stream);
 
 /*
  * Soft-prune gradient mask: out = grad * keep along one axis.

@@ -22,6 +22,7 @@ ERR_NO_DEVICE = -5
 
 F32, BF16, F16 = 0, 1, 2
 SIGMA_IDS = {"softplus": 0, "sigmoid": 1, "exp": 2, "relu": 3}
+FIXED_SIGMA_IDS = dict(SIGMA_IDS, tanh_shift=4)      # the fixed-tau weights add tanh_shift
 PATH_AUTO, PATH_PRECISE, PATH_TENSOR = 0, 1, 2
 WTA_THRESHOLD, WTA_EXACT_K = 0, 1
 WTA_GELU_INPUT = 0x100
@@ -86,6 +87,8 @@ SIGNATURES = {
     "tau_column_sum_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "tau_column_sum": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _i32, _vp, ctypes.c_size_t, _vp]),
     "tau_grad_mask": (ctypes.c_int, [_vp, _i32, _i64, _i64, _vp, _i32, _vp, _vp]),
+    "tau_opus_fixed_fwd": (ctypes.c_int, [_vp, _i64, _i64, _i64, _vp, _i64, _i64, _i32, _vp, _vp]),
+    "tau_opus_fixed_bwd": (ctypes.c_int, [_vp, _vp, _i64, _i64, _i64, _vp, _i64, _i64, _i32, _vp, _vp]),
     "tau_cross_entropy_fwd": (ctypes.c_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
     "tau_cross_entropy_bwd": (ctypes.c_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp]),
 }

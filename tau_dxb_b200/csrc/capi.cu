@@ -59,6 +59,10 @@ int tau_star_analytic_impl(const float*, int64_t, int64_t, int64_t, int32_t, flo
 size_t layer_norm_bwd_workspace(int64_t M, int64_t N);
 size_t column_sum_workspace(int64_t M, int64_t N);
 int grad_mask_impl(const void*, int32_t, int64_t, int64_t, const uint8_t*, int32_t, void*, cudaStream_t);
+int fixed_fwd_impl(const float*, int64_t, int64_t, int64_t, const float*, int64_t, int64_t, int32_t, float*,
+                   cudaStream_t);
+int fixed_bwd_impl(const float*, const float*, int64_t, int64_t, int64_t, const float*, int64_t, int64_t, int32_t,
+                   float*, cudaStream_t);
 int column_sum_impl(const void*, int32_t, int64_t, int64_t, void*, int32_t, void*, size_t, cudaStream_t);
 int cross_entropy_fwd_impl(const void*, int64_t, int64_t, const int64_t*, int64_t, float*, float*, cudaStream_t);
 int cross_entropy_bwd_impl(const void*, int64_t, int64_t, const int64_t*, int64_t, const float*, const float*, void*,
@@ -289,6 +293,21 @@ int tau_layer_norm_bwd(const void* dy, int32_t dy_dtype, const float* x, const f
   g_last_error[0] = 0;
   return layer_norm_bwd_impl(dy, dy_dtype, x, mean, rstd, gamma, M, d, dx, dgamma, dbeta, workspace,
                              workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int tau_opus_fixed_fwd(const float* scores, int64_t rows, int64_t L, int64_t row_stride, const float* tau,
+                       int64_t n_tau, int64_t rows_per_tau, int32_t sigma_id, float* attn, void* stream) {
+  g_last_error[0] = 0;
+  return fixed_fwd_impl(scores, rows, L, row_stride, tau, n_tau, rows_per_tau, sigma_id, attn,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int tau_opus_fixed_bwd(const float* scores, const float* grad_attn, int64_t rows, int64_t L, int64_t row_stride,
+                       const float* tau, int64_t n_tau, int64_t rows_per_tau, int32_t sigma_id, float* grad_scores,
+                       void* stream) {
+  g_last_error[0] = 0;
+  return fixed_bwd_impl(scores, grad_attn, rows, L, row_stride, tau, n_tau, rows_per_tau, sigma_id, grad_scores,
+                        static_cast<cudaStream_t>(stream));
 }
 
 int tau_grad_mask(const void* grad, int32_t dtype, int64_t rows, int64_t cols, const uint8_t* keep, int32_t axis,

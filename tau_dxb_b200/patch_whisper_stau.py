@@ -6,6 +6,8 @@ Same public functions as the reference module echo/patch_whisper_stau.py:
   remove_stau(model)                                    (:408-415)
   load_tau_dict(json_path)                              (:150-183)
   STauOpusLearnable(n_heads, sigma_name)                (:115-133)
+  apply_fixed_stau(model, tau_source, sigma_name)       (:279-322)
+  STauOpusMaxStableFn.apply(scores, tau, sigma_name)    (:74-112)
   _classify_attn, _parse_layer_idx, _log_tau_for_init   (:140-147, :274-276, :267-271)
 
 Every WhisperAttention module gets a `_stau_opus` submodule owning per-head
@@ -124,6 +126,112 @@ def _log_tau_for_init(tau: float) -> float:
     if tau <= 1.001:
         return -8.0
     return math.log(math.exp(tau - 1.0) - 1.0)
+
+
+class STauOpusMaxStableFn(torch.autograd.Function):
+    """Fixed-tau attention weights from materialised scores
+    (echo/patch_whisper_stau.py:74-112): x = s - max(s), q = max(sigma(x),
+    1e-8)^tau, attn = q / max(sum q, 1e-8), and the score gradient with the
+    max shift's correction at the row's first argmax. The operator of the
+    fixed-tau patch. Runs on tau_opus_fixed_fwd / tau_opus_fixed_bwd (one warp
+    per row, fp32). tau: a number or a per-head tensor of shape (1, H, 1, 1)
+    for [B, H, Lq, Lk] scores; sigma_name adds 'tanh_shift' to the four sigmas
+    of the fused operator. CUDA tensors only."""
+
+    @staticmethod
+    def forward(ctx, scores, tau, sigma_name):
+        from . import _capi as C
+        sid = C.FIXED_SIGMA_IDS[sigma_name]
+        if not scores.is_cuda:
+            raise RuntimeError("tau_dxb_b200: STauOpusMaxStableFn runs on CUDA tensors only")
+        s = scores.float().contiguous()
+        L = s.shape[-1]
+        rows = s.numel() // L if L else 0
+        if torch.is_tensor(tau):
+            tv = tau.detach().reshape(-1).to(device=s.device, dtype=torch.float32).contiguous()
+        else:
+            tv = torch.full((1,), float(tau), dtype=torch.float32, device=s.device)
+        if tv.numel() == 1:
+            rows_per_tau = 1
+        elif s.dim() == 4 and tv.numel() == s.shape[1]:
+            rows_per_tau = s.shape[2]          # [B, H, Lq, Lk] with a per-head tau
+        else:
+            raise ValueError(f"tau with {tv.numel()} values does not match scores of shape {tuple(s.shape)}")
+        attn = torch.empty_like(s)
+        rc = C.lib().tau_opus_fixed_fwd(s.data_ptr(), rows, L, L, tv.data_ptr(), tv.numel(), rows_per_tau, sid,
+                                        attn.data_ptr(), C.stream_ptr(s.device))
+        C.check("tau_opus_fixed_fwd", rc)
+        ctx.save_for_backward(s, tv)
+        ctx.meta = (sid, rows, L, rows_per_tau)
+        return attn
+
+    @staticmethod
+    def backward(ctx, grad_attn):
+        from . import _capi as C
+        s, tv = ctx.saved_tensors
+        sid, rows, L, rows_per_tau = ctx.meta
+        g = grad_attn.float().contiguous()
+        ds = torch.empty_like(s)
+        rc = C.lib().tau_opus_fixed_bwd(s.data_ptr(), g.data_ptr(), rows, L, L, tv.data_ptr(), tv.numel(),
+                                        rows_per_tau, sid, ds.data_ptr(), C.stream_ptr(s.device))
+        C.check("tau_opus_fixed_bwd", rc)
+        return ds, None, None
+
+
+def _make_fixed_stau_forward():
+    """transformers' eager attention with the fixed-tau weights
+    (echo/patch_whisper_stau.py:190-214): scores = q k^T * scaling (+ mask) as
+    the projections' dtype computes them, the weights in fp32 from the module's
+    _stau_tau / _stau_sigma, dropout, then the weights (cast back) times v.
+    Returns the weights as well, as the reference does."""
+    def stau_eager_attention_forward(module, query, key, value, attention_mask, scaling=None,
+                                     dropout=0.0, **kwargs):
+        if scaling is None:
+            scaling = query.size(-1) ** -0.5
+        scores = torch.matmul(query, key.transpose(2, 3)) * scaling
+        if attention_mask is not None:
+            scores = scores + attention_mask
+        tau = getattr(module, "_stau_tau", None)
+        tau = 1.0 if tau is None else tau.to(scores.device)
+        sigma_name = getattr(module, "_stau_sigma", "softplus")
+        weights = STauOpusMaxStableFn.apply(scores.float(), tau, sigma_name)
+        weights = F.dropout(weights, p=dropout, training=module.training)
+        out = torch.matmul(weights.to(value.dtype), value)
+        return out.transpose(1, 2).contiguous(), weights.to(value.dtype)
+    return stau_eager_attention_forward
+
+
+def apply_fixed_stau(model, tau_source, sigma_name="softplus"):
+    """Give every WhisperAttention a fixed per-head tau
+    (echo/patch_whisper_stau.py:279-322). tau_source: a number (every head), a
+    dict {"encoder_self": {layer: [H taus]}, ...}, or the path of a tau* JSON;
+    sigma_name: one name or a dict per site kind. Heads without an entry get
+    tau = 1. Sets module._stau_tau ((1, H, 1, 1) fp32) and module._stau_sigma,
+    and swaps transformers' eager attention for the fixed-tau one."""
+    if isinstance(tau_source, (str, Path)):
+        tau_dict = load_tau_dict(tau_source)
+    elif isinstance(tau_source, dict):
+        tau_dict = tau_source
+    elif isinstance(tau_source, (float, int)):
+        tau_dict = None
+        scalar_tau = float(tau_source)
+    else:
+        raise TypeError(f"Unsupported tau_source type: {type(tau_source)}")
+    sigma_map = _sigma_map(sigma_name)
+    for name, module in model.named_modules():
+        if module.__class__.__name__ != "WhisperAttention":
+            continue
+        h = module.num_heads
+        kind = _classify_attn(name, module)
+        if tau_dict is not None:
+            tau_list = tau_dict.get(kind, {}).get(_parse_layer_idx(name), [1.0] * h)
+            tau_tensor = torch.tensor(tau_list, dtype=torch.float32).view(1, h, 1, 1)
+        else:
+            tau_tensor = torch.full((1, h, 1, 1), scalar_tau, dtype=torch.float32)
+        module._stau_tau = tau_tensor
+        module._stau_sigma = sigma_map[kind]
+        module.__dict__.pop("forward", None)      # transformers' own forward calls the eager function
+    whisper_module.eager_attention_forward = _make_fixed_stau_forward()
 
 
 def _make_learnable_stau_forward():

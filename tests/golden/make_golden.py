@@ -82,6 +82,40 @@ def make_attn(ref):
         print("wrote", name)
 
 
+def make_maxstable(ref):
+    """STauOpusMaxStableFn of the fixed-tau patch (echo/patch_whisper_stau.py:74-112):
+    attention weights from materialised scores and their gradient, every sigma
+    of that module's registry, a per-head tau tensor and a scalar tau."""
+    import patch_whisper_stau as P
+    out = {}
+    cases = [("softplus", "head"), ("sigmoid", "head"), ("exp", "head"), ("relu", "head"),
+             ("tanh_shift", "head"), ("softplus", "scalar"), ("exp", "scalar")]
+    for ci, (sg, tk) in enumerate(cases):
+        g = torch.Generator().manual_seed(400 + ci)
+        B, H, Lq, Lk = 2, 3, 17, 45
+        scores = torch.randn(B, H, Lq, Lk, generator=g) * 3.0
+        if ci == 0:       # a causal additive mask, as the decoder passes it
+            scores = scores + torch.full((Lq, Lk), torch.finfo(torch.float32).min).triu(Lk - Lq + 1)
+        if tk == "head":
+            tau = (1.0 + torch.rand(H, generator=g) * 2.5).view(1, H, 1, 1)
+        else:
+            tau = 1.7
+        dO = torch.randn(B, H, Lq, Lk, generator=g)
+        sc = scores.clone().requires_grad_()
+        attn = P.STauOpusMaxStableFn.apply(sc, tau, sg)
+        attn.backward(dO)
+        out[f"c{ci}_sigma"] = np.array(sg)
+        out[f"c{ci}_scores"] = scores.numpy()
+        out[f"c{ci}_tau"] = np.asarray(tau.reshape(-1).numpy() if torch.is_tensor(tau) else [tau], dtype=np.float32)
+        out[f"c{ci}_tau_is_tensor"] = np.array(torch.is_tensor(tau))
+        out[f"c{ci}_dO"] = dO.numpy()
+        out[f"c{ci}_attn"] = attn.detach().numpy()
+        out[f"c{ci}_dscores"] = sc.grad.numpy()
+    out["n_cases"] = np.array(len(cases))
+    np.savez_compressed(os.path.join(HERE, "maxstable.npz"), **out)
+    print("wrote maxstable")
+
+
 def make_wta(ref):
     import triton_wta as T
     import patch_whisper_sparse_grad as S
@@ -220,6 +254,7 @@ def main(argv):
     make_k_table(ref)
     make_lr_table(ref)
     make_tau_star(ref)
+    make_maxstable(ref)
 
 
 if __name__ == "__main__":

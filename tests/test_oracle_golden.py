@@ -154,3 +154,17 @@ def test_tau_star_oracle_matches_reference_golden():
         rtol = 2e-3 if T <= 2 else 2e-5
         assert np.allclose(tau, z[k + "_tau"], rtol=rtol, atol=2e-5), (ci, np.abs(tau - z[k + "_tau"]).max())
         assert np.allclose(kl, z[k + "_kl"], rtol=1e-3, atol=2e-6), (ci, np.abs(kl - z[k + "_kl"]).max())
+
+
+def test_fixed_tau_oracle_matches_reference():
+    """oracle.stau_fixed against STauOpusMaxStableFn's own outputs
+    (echo/patch_whisper_stau.py:74-112): every sigma, per-head and scalar tau."""
+    from oracle import stau_fixed as OF
+    g = _load(os.path.join(GOLDEN, "maxstable.npz"))
+    for ci in range(int(g["n_cases"])):
+        sg = str(g[f"c{ci}_sigma"])
+        sc, tau, dO = g[f"c{ci}_scores"], g[f"c{ci}_tau"], g[f"c{ci}_dO"]
+        attn = OF.forward(sc, tau, sg)
+        assert rel_err(attn, g[f"c{ci}_attn"]) < 2e-6, (ci, sg)
+        ds = OF.backward(sc, tau, sg, dO)
+        assert rel_err(ds, g[f"c{ci}_dscores"]) < 2e-5, (ci, sg, rel_err(ds, g[f"c{ci}_dscores"]))
