@@ -231,11 +231,16 @@ __device__ __forceinline__ uint32_t gelu_bf16x2(uint32_t w) {
 
 // Blocks per SM the register budget is sized for: two rows (this one and the
 // prefetched next) take 8*CH registers per thread.
-template <int CH, bool HIST, bool GELU = false>
-constexpr int fwd16_min_blocks() { return CH > 12 ? 2 : (CH == 12 && (HIST || GELU) ? 3 : 4); }
+// Without the prefetch (PF = false: launches with few rows per warp, where a
+// prefetch has little to overlap) one row takes 4*CH registers, so more warps
+// fit per SM to hide the search's dependent probes.
+template <int CH, bool HIST, bool GELU = false, bool PF = true>
+constexpr int fwd16_min_blocks() {
+  return !PF ? (CH > 12 ? 3 : 6) : (CH > 12 ? 2 : (CH == 12 && (HIST || GELU) ? 3 : 4));
+}
 
-template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST, bool GELU = false>
-__global__ void __launch_bounds__(kFastWarps * 32, fwd16_min_blocks<CH, HIST, GELU>())
+template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST, bool GELU = false, bool PF = true>
+__global__ void __launch_bounds__(kFastWarps * 32, fwd16_min_blocks<CH, HIST, GELU, PF>())
 wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_stride,
                  int k_host, const int32_t* __restrict__ k_dev,
                  uint16_t* __restrict__ y, uint8_t* __restrict__ bitmask,
@@ -257,8 +262,8 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
 
   const int64_t stride_rows = static_cast<int64_t>(gridDim.x) * kFastWarps;
   int64_t row = static_cast<int64_t>(blockIdx.x) * kFastWarps + warp;
-  uint4 nxt[CH];
-  if (row < n_rows) {
+  uint4 nxt[PF ? CH : 1];
+  if (PF && row < n_rows) {
     const uint4* src = reinterpret_cast<const uint4*>(x + row * row_stride);
 #pragma unroll
     for (int c = 0; c < CH; ++c) nxt[c] = __ldcs(src + c * 32 + lane);
@@ -287,8 +292,14 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
   }
   for (; row < n_rows; row += stride_rows) {
     uint4 w[CH];
+    if constexpr (PF) {
 #pragma unroll
-    for (int c = 0; c < CH; ++c) w[c] = nxt[c];
+      for (int c = 0; c < CH; ++c) w[c] = nxt[c];
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(x + row * row_stride);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) w[c] = __ldcs(src + c * 32 + lane);
+    }
     if constexpr (GELU) {     // the row is the pre-activation: select on gelu(x)
       static_assert(BF, "GELU input is bf16 only");
 #pragma unroll
@@ -297,7 +308,7 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
     }
     // prefetch the next row while this one is selected
     const int64_t nrow = row + stride_rows;
-    if (nrow < n_rows) {
+    if (PF && nrow < n_rows) {
       const uint4* src = reinterpret_cast<const uint4*>(x + nrow * row_stride);
 #pragma unroll
       for (int c = 0; c < CH; ++c) nxt[c] = __ldcs(src + c * 32 + lane);
@@ -335,26 +346,28 @@ wta_fwd16_kernel(const uint16_t* __restrict__ x, int64_t n_rows, int64_t row_str
       // t_prev +- |c0 - k| * ipc, which usually lands on or next to the
       // answer; then gallop from the bracket edge it set, and bisect
       c0 = count_ge(t_prev, BoolC<true>{});
-      const float dest = fminf(static_cast<float>(abs(c0 - k)) * ipc + 0.5f, 256.f);
-      const uint32_t d = max(1u, static_cast<uint32_t>(dest));
+      // the linear estimate only where keys near the threshold are dense in
+      // count (a few keys per count at most); elsewhere (thresholds near 0,
+      // where keys spread over many exponents) step 1 and gallop
+      // (d = 0: no estimate probe, gallop from t_prev at once)
+      const uint32_t d = ipc <= 2.f
+          ? max(1u, static_cast<uint32_t>(fminf(static_cast<float>(abs(c0 - k)) * ipc + 0.5f, 64.f))) : 0u;
       bool up;
       if (c0 >= k) {
         lo = t_prev;
-        const uint32_t p = lo + d < hi ? lo + d : hi - 1;
         up = true;
-        if (p > lo) {
+        const uint32_t p = lo + d < hi ? lo + d : hi - 1;
+        if (d > 0 && p > lo) {
           if (count_ge(p, BoolC<true>{}) >= k) lo = p;
           else { hi = p; up = false; }
         }
       } else {
         hi = t_prev;
-        const uint32_t p = hi - kNeg > d ? hi - d : kNeg;
         up = false;
-        if (p < hi && p > kNeg) {
+        const uint32_t p = hi - kNeg > d ? hi - d : kNeg;
+        if (d > 0 && p < hi && p > kNeg) {
           if (count_ge(p, BoolC<true>{}) >= k) { lo = p; up = true; }
           else hi = p;
-        } else {
-          lo = kNeg;
         }
       }
       if (up) {            // the answer is at lo or above: walk up
@@ -636,6 +649,12 @@ template <int CH, bool BF, bool EXACT, bool WRITE_Y, bool HIST, bool GELU = fals
 int launch_fwd16(const void* x, int64_t n_rows, int64_t row_stride, int k, const int32_t* k_dev,
                  void* y, uint8_t* bitmask, int32_t* win, cudaStream_t st) {
   auto kern = wta_fwd16_kernel<CH, BF, EXACT, WRITE_Y, HIST, GELU>;
+  if constexpr (!HIST && !GELU) {
+    // few rows per warp at the prefetching kernel's occupancy (4 blocks per
+    // SM): the variant without prefetch runs more warps instead
+    if (n_rows < static_cast<int64_t>(sm_count()) * 4 * kFastWarps * 4)
+      kern = wta_fwd16_kernel<CH, BF, EXACT, WRITE_Y, HIST, GELU, false>;
+  }
   const size_t smem = HIST ? 256 * CH * 4 : 0;
   if (smem) TDX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;

@@ -92,20 +92,23 @@ def test_exact_k_tie_order_vs_torch_topk_cuda(W):
         assert bool(same_rows.all()), (k, int((~same_rows).sum()), int(tie_rows.sum()))
 
 
-@pytest.mark.parametrize("k", [154, 306, 307, 768, 1536])
-def test_full_size_encoder_threshold_vs_torch(W, k):
+@pytest.mark.parametrize("rows,k", [(24000, 154), (24000, 306), (24000, 307), (24000, 768), (24000, 1536),
+                                    (7168, 306), (7168, 1536)])
+def test_full_size_encoder_threshold_vs_torch(W, rows, k):
+    """Encoder [24000, 3072] and decoder [7168, 3072] sizes (the decoder's takes
+    the kernel variant without row prefetch)."""
     g = torch.Generator(device=DEV).manual_seed(k)
-    x = torch.nn.functional.gelu(torch.randn(24000, 3072, device=DEV, generator=g)).to(torch.bfloat16)
+    x = torch.nn.functional.gelu(torch.randn(rows, 3072, device=DEV, generator=g)).to(torch.bfloat16)
     y, bits = W.wta_select(x, k, W.THRESHOLD)
     thr = x.float().kthvalue(3072 - k + 1, dim=-1, keepdim=True).values
     keep = x.float() >= thr
     assert torch.equal(W.unpack_mask(bits, 3072), keep)
     assert torch.equal(y, torch.where(keep, x, torch.zeros_like(x)))
     # oracle on a sample of rows
-    rows = slice(0, 256)
-    ref = OW.threshold_mask(x[rows].float().cpu().numpy(), k)
-    assert np.array_equal(W.unpack_mask(bits[rows], 3072).cpu().numpy(), ref)
-    dy = torch.randn(24000, 3072, device=DEV, generator=g).to(torch.bfloat16)
+    sample = slice(0, 256)
+    ref = OW.threshold_mask(x[sample].float().cpu().numpy(), k)
+    assert np.array_equal(W.unpack_mask(bits[sample], 3072).cpu().numpy(), ref)
+    dy = torch.randn(rows, 3072, device=DEV, generator=g).to(torch.bfloat16)
     dx = W.wta_backward(dy, bits)
     assert torch.equal(dx, dy * keep.to(dy.dtype))
 
