@@ -94,11 +94,11 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                 "-lms", "20", "-i", str(self.gpu)], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
-        time.sleep(0.15)
+        time.sleep(0.1)
         return self
 
     def __exit__(self, *exc):
@@ -113,24 +113,29 @@ class ClockSampler:
             self.lines = [l for l in out.splitlines() if l.strip()]
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
+        """Median SM clock over the samples taken under load (power draw in the
+        upper half of the range seen; all samples when the range is flat),
+        and every throttle reason seen at all."""
+        rows, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for l in getattr(self, "lines", []):
             f = [x.strip() for x in l.split(",")]
             if len(f) < 9:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
+                sm, mx, pw = float(f[1]), float(f[2]), float(f[3])
             except ValueError:
                 continue
+            rows.append((sm, pw))
             for n, v in zip(names, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
-        if not sm:
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        lo, hi = min(p for _, p in rows), max(p for _, p in rows)
+        load = [s for s, p in rows if hi - lo < 50 or p >= (lo + hi) / 2]
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(rows), "samples_under_load": len(load), "power_w_max": hi}
 
 
 # ---------------------------------------------------------------- our arm
