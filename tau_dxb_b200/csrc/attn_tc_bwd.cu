@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
         const bool q_ok = (qt0 + i) * kT + r < p.Lq;
         st[r] = q_ok ? -m4[u] * al2 : 0.f;
         st[kT + r] = q_ok ? 1.f / z4[u] : 0.f;
-        st[2 * kT + r] = q_ok ? d4[u] : 0.f;
+        st[2 * kT + r] = q_ok ? -d4[u] : 0.f;       // -D: t = P (dP + (-D)), no negation per score
       }
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars->qd_full[s]);
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     // ---------------------------------------------------------------- elementwise
     // Per score: a2 = log2(e) alpha (s scale - m), y = tau log2 sigma,
     // q = 2^max(y, ylo) (both clamps of the reference in one), P = q / Z,
-    // t = P (dP - D), F / (tau alpha) = t sigma'/sigma.
+    // t = P (dP - D) (the statistics hold -D), F / (tau alpha) = t sigma'/sigma.
     // Sums kept scaled: acc_tau = sum t tau log2 sigma_clamped and
     // acc_alpha = sum t clip(ratio a2, +-30 log2(e) alpha); the constants are
     // divided out once per CTA.
@@ -568,18 +568,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
             if constexpr (kClean) P = tc::mul2(make_float2(tc::ex2(y.x), tc::ex2(y.y)), rz);
             else P = tc::mul2(make_float2(tc::ex2(fmaxf(y.x, ylo)), tc::ex2(fmaxf(y.y, ylo))), rz);
             if constexpr (!kFull) P = tc::mul2(P, kmask2);
-            const float2 t = tc::mul2(P, tc::sub2(make_float2(__uint_as_float(rr[16 + e]),
+            const float2 t = tc::mul2(P, tc::add2(make_float2(__uint_as_float(rr[16 + e]),
                                                               __uint_as_float(rr[17 + e])), dq));
-            // x = s - rowmax <= 0, so ratio * a2 <= 0: only the lower clip can act
-            const float2 ra = tc::mul2(ratio, a2);
+            const float2 F = tc::mul2(t, ratio);
             if constexpr (kClean) {
+              // no clip can act: t ratio a2 = F a2
               acc_tau = tc::fma2(t, y, acc_tau);
-              acc_alpha = tc::fma2(t, ra, acc_alpha);
+              acc_alpha = tc::fma2(F, a2, acc_alpha);
             } else {
+              // x = s - rowmax <= 0, so ratio * a2 <= 0: only the lower clip can act
+              const float2 ra = tc::mul2(ratio, a2);
               acc_tau = tc::fma2(t, make_float2(fmaxf(y.x, ytau), fmaxf(y.y, ytau)), acc_tau);
               acc_alpha = tc::fma2(t, make_float2(fmaxf(ra.x, -glim), fmaxf(ra.y, -glim)), acc_alpha);
             }
-            const float2 F = tc::mul2(t, ratio);
             pp[e >> 1] = tc::pack_bf16(P.x, P.y);
             pf[e >> 1] = tc::pack_bf16(F.x, F.y);
           }
