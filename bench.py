@@ -512,6 +512,27 @@ def write_step_profile(torch, step, batch, path):
         f.write("\n".join(lines) + "\n")
 
 
+def step_phase_times(torch, step, batches, world, n=5):
+    """Per-phase device time of n more replayed steps (outside the timed
+    region), each phase's mean over the steps and then its max over the ranks:
+    fwd_bwd (graph A), all_reduce (the NCCL call between the graphs; world > 1)
+    and update (graph B)."""
+    import torch.distributed as dist
+    step.phase_events = []
+    for i in range(n):
+        step.step(*batches[i % 2])
+    torch.cuda.synchronize()
+    recs, step.phase_events = step.phase_events, None
+    names = ["fwd_bwd", "all_reduce", "update"] if world > 1 else ["fwd_bwd", "update"]
+    if not recs or any(k not in r for r in recs for k in names):
+        return None
+    v = torch.tensor([statistics.mean(r[k][0].elapsed_time(r[k][1]) for r in recs) for k in names],
+                     device=torch.cuda.current_device())
+    if world > 1:
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    return {k: round(float(x), 3) for k, x in zip(names, v.tolist())}
+
+
 def train_sub_bench(torch, device, world, rank, steps=10, warmup=3, profile_path=""):
     """Whisper-small tau-opus + WTA train step (batch 16 per GPU, bf16 autocast,
     fp32 master weights, AdamW); one NCCL all-reduce of all gradients per step
@@ -543,7 +564,8 @@ def train_sub_bench(torch, device, world, rank, steps=10, warmup=3, profile_path
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    if profile_path and rank == 0:
+    phases = step_phase_times(torch, step, batches, world)
+    if profile_path and rank == 0 and world == 1:
         write_step_profile(torch, step, batches[0], profile_path)
     flops = T.model_flops_per_step(cfg)
     peak = load_peaks()[2]
@@ -552,11 +574,13 @@ def train_sub_bench(torch, device, world, rank, steps=10, warmup=3, profile_path
            "model_tflop_per_step_per_gpu": round(flops / 1e12, 3),
            "mfu_of_sustained_bf16": round(flops / (ms * 1e-3) / (peak * 1e12), 4),
            "skipped_steps": step.skipped,
-           "parallelism": f"dp{world} (one NCCL all-reduce of the flat fp32 gradient buffer between the "
-                          "step's two CUDA graphs)" if world > 1 else "single GPU (two CUDA graphs)",
+           "parallelism": f"dp{world} (fp32 gradients averaged over NCCL in ~64 MB coalesced buckets from "
+                          "inside the backward, captured in the step's first CUDA graph)" if world > 1
+                          else "single GPU (two CUDA graphs)",
            "parallelism_short": f"dp{world}",
-           "data": "synthetic log-mel N(0,1) [16,80,3000], labels uniform over 51865, lengths U[64,448]"}
-    step.reset_graph()       # graphs released before the process group is destroyed
+           "data": "synthetic log-mel N(0,1) [16,80,3000], labels uniform over 51865, lengths U[64,448]",
+           "phases_ms": phases}
+    step.close()             # graphs released before the process group is destroyed
     del step
     torch.cuda.empty_cache()
     return out
@@ -889,7 +913,7 @@ def run_ours(args, rank, world, local_rank):
         ts = result.pop("train_step")
         result["train_step_detail"] = ts
         result["train_step"] = {k: ts[k] for k in ("samples_per_s", "ms_per_step", "n_gpus", "global_batch",
-                                                   "mfu_of_sustained_bf16", "parallelism_short")}
+                                                   "mfu_of_sustained_bf16", "parallelism_short", "phases_ms")}
     return result
 
 

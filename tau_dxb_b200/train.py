@@ -265,16 +265,22 @@ class TrainStep:
                                                                                 "decoder_layerdrop", 0.0)
         self.graphed = bool(cuda_graph) and self.device.type == "cuda" and cfg.grad_accum == 1 \
             and not layerdrop
-        # With more than one rank, the graphed step all-reduces one flat fp32
-        # gradient buffer between its two graphs (every .grad is a view of it);
-        # otherwise DistributedDataParallel reduces bucket by bucket.
+        # With more than one rank, the graphed step averages the gradients over
+        # NCCL in buckets from inside the backward (captured in graph A); over
+        # other backends it all-reduces one flat fp32 gradient buffer between
+        # its two graphs (every .grad a view of it). Ungraphed, it is
+        # DistributedDataParallel.
         self._flat = None
         self._reduce_avg = False
+        self._buckets = None            # in-backward gradient buckets (NCCL), see _init_buckets
+        self._reduced_in_backward = False
         if self.world > 1:
             if self.graphed:
                 for t in list(self.net.parameters()) + list(self.net.buffers()):
                     dist.broadcast(t.data, src=0)        # the replicas start identical, as DDP makes them
                 self._reduce_avg = dist.get_backend() == "nccl"
+                if self._reduce_avg:
+                    self._init_buckets(bucket_mb)
             else:
                 from torch.nn.parallel import DistributedDataParallel as DDP
                 self.net = DDP(self.net, device_ids=[self.device.index] if self.device.type == "cuda" else None,
@@ -297,6 +303,9 @@ class TrainStep:
         if self.lagged:
             self._flag_host = torch.zeros(1, dtype=torch.float32).pin_memory()
         self.graph_warmup = 2           # eager steps (on a side stream) before the capture
+        # When a list, every replayed step appends {phase: (start, end)} CUDA
+        # events: "fwd_bwd" (graph A), "all_reduce" (world > 1), "update" (graph B)
+        self.phase_events = None
         self.reset_graph()
 
     def reset_graph(self):
@@ -306,6 +315,14 @@ class TrainStep:
         self._gA = self._gB = None
         self._eager_calls = 0
         self._static = None
+
+    def close(self):
+        """Release the captured graphs (before destroy_process_group when they
+        hold NCCL calls) and the gradient hooks."""
+        self.reset_graph()
+        for h in getattr(self, "_hook_handles", ()):
+            h.remove()
+        self._hook_handles = []
     @property
     def skipped(self) -> int:
         """Steps skipped for a non-finite loss (settles the last step first)."""
@@ -412,16 +429,27 @@ class TrainStep:
     # ---- data parallel over a flat gradient buffer (graphed, world > 1) ----
 
     def _dp_local(self, mel, labels):
-        """Forward and backward into the flat gradient buffer (zeroed first);
-        the last slot of the buffer carries this rank's non-finite-loss flag
-        through the all-reduce."""
-        if self._flat is None:
+        """Forward and backward. With buckets (NCCL), the gradients stay where
+        autograd puts them and are averaged bucket by bucket while the backward
+        runs, this rank's non-finite-loss flag riding with the first bucket.
+        Otherwise they go into the flat buffer (zeroed first), whose last slot
+        carries the flag through the all-reduce after the backward."""
+        if self._buckets is not None:
+            self.opt.zero_grad(set_to_none=True)
+            loss, _ = self.loss(mel, labels)
+            self._flag.copy_((~torch.isfinite(loss.detach())).float().reshape(1))
+            self._bucket_begin()
+            loss.backward()
+            self._bucket_end()
+            return loss.detach()
+        first = self._flat is None
+        if first:
             self.opt.zero_grad(set_to_none=True)
         else:
             self._flat.zero_()
         loss, _ = self.loss(mel, labels)
         loss.backward()
-        if self._flat is None:
+        if first:
             self._build_flat()
         self._flat[-1:].copy_((~torch.isfinite(loss.detach())).float().reshape(1))
         return loss.detach()
@@ -442,28 +470,131 @@ class TrainStep:
             off += p.numel()
         self._flat = flat
 
+    # ---- gradient buckets averaged inside the backward (NCCL) ----
+
+    def _init_buckets(self, bucket_mb: int):
+        """Hooks that see each parameter's gradient finished. The first
+        backward records the order in which they finish and is averaged in one
+        coalesced call after it; later ones average a bucket (about bucket_mb
+        MB of gradients, in that order) as soon as its last gradient is in:
+        one coalesced NCCL call per bucket on NCCL's stream, overlapping the
+        rest of the backward. The calls run on the autograd thread in the
+        same order on every rank, and are captured in graph A."""
+        self._bucket_bytes = max(1, int(bucket_mb)) << 20
+        self._pg = dist.group.WORLD
+        self._ready_order = []
+        self._buckets = []
+        self._pbucket = {}
+        self._works = []
+        self._bucket_open = False
+        self._flag_pending = False
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self._hook_handles = [p.register_post_accumulate_grad_hook(self._grad_ready)
+                              for p in self.model.parameters() if p.requires_grad]
+
+    def _build_buckets(self):
+        """Cut the recorded order into buckets of about bucket_bytes."""
+        buckets, cur, size = [], [], 0
+        seen = set()
+        for p in self._ready_order:
+            if id(p) in seen:
+                continue
+            seen.add(id(p))
+            self._pbucket[id(p)] = len(buckets)
+            cur.append(p)
+            size += p.numel() * 4
+            if size >= self._bucket_bytes:
+                buckets.append({"params": cur, "seen": 0, "issued": False})
+                cur, size = [], 0
+        if cur:
+            buckets.append({"params": cur, "seen": 0, "issued": False})
+        self._buckets = buckets
+
+    def _grad_ready(self, p):
+        if not self._bucket_open:
+            if self._recording:
+                self._ready_order.append(p)
+            return
+        b = self._pbucket.get(id(p))
+        if b is None:
+            return
+        bk = self._buckets[b]
+        bk["seen"] += 1
+        if bk["seen"] == len(bk["params"]):
+            self._issue_bucket(bk)
+
+    def _issue_bucket(self, bk):
+        bk["issued"] = True
+        tensors = [p.grad for p in bk["params"] if p.grad is not None]
+        if self._flag_pending:
+            tensors.append(self._flag)
+            self._flag_pending = False
+        if tensors:
+            self._works.append(self._allreduce_avg(tensors))
+
+    def _allreduce_avg(self, tensors):
+        opts = dist.AllreduceCoalescedOptions()
+        opts.reduceOp = dist.ReduceOp.AVG
+        opts.asyncOp = True
+        return self._pg.allreduce_coalesced(tensors, opts)
+
+    @property
+    def _recording(self):
+        return not self._buckets
+
+    def _bucket_begin(self):
+        self._flag_pending = True
+        if self._recording:
+            return                       # the first backward only records the order
+        for bk in self._buckets:
+            bk["seen"], bk["issued"] = 0, False
+        self._bucket_open = True
+
+    def _bucket_end(self):
+        """Average what the backward did not (all of it the first time; a
+        bucket some of whose parameters got no gradient), in bucket order, then
+        make the current stream wait for every reduction."""
+        self._bucket_open = False
+        if self._recording:
+            self._build_buckets()
+        for bk in self._buckets:
+            if not bk["issued"]:
+                self._issue_bucket(bk)
+        if self._flag_pending:
+            self._issue_bucket({"params": []})
+        for w in self._works:
+            w.wait()
+        self._works = []
+        self._reduced_in_backward = True
+
     def _dp_reduce(self):
         """Average the gradients over the ranks (the flag slot becomes the
         fraction of ranks with a non-finite loss). NCCL averages in the
-        collective; other backends sum, and the step scales afterwards."""
+        collective; other backends sum, and the step scales afterwards. A
+        no-op when the buckets already did it inside the backward."""
+        if self._reduced_in_backward:
+            return
         dist.all_reduce(self._flat, op=dist.ReduceOp.AVG if self._reduce_avg else dist.ReduceOp.SUM)
 
     def _dp_finish(self):
         """Scale (when the collective summed), the flag of the whole job as a
         0-dim tensor, and clipping; returns the flag."""
-        if not self._reduce_avg:
-            self._flat.mul_(1.0 / self.world)
-        bad = (self._flat[-1] > 0).float()
+        if self._buckets is not None:
+            bad = (self._flag[0] > 0).float()
+        else:
+            if not self._reduce_avg:
+                self._flat.mul_(1.0 / self.world)
+            bad = (self._flat[-1] > 0).float()
         torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.clip)
         return bad
 
     def _step_graphed_dp(self, mel, labels):
         """The graphed step on each of several ranks: graph A = forward and
-        backward into the flat gradient buffer; then one all-reduce of the
-        buffer, issued between the replays (no collective inside a graph);
-        graph B = scaling, flag, clipping and the AdamW update. The previous
-        step is settled while A and the all-reduce run, before B changes the
-        weights."""
+        backward, with the gradient average inside it (NCCL buckets issued
+        from the backward) or, over other backends, one all-reduce of the flat
+        gradient buffer issued between the replays; graph B = scaling, flag,
+        clipping and the AdamW update. The previous step is settled while A
+        runs, before B changes the weights."""
         if self._gA is None and self._eager_calls < self.graph_warmup:
             self._eager_calls += 1
             side = torch.cuda.Stream(self.device)
@@ -496,12 +627,34 @@ class TrainStep:
                 self.opt.step()
             self._gA, self._gB = gA, gB
         self._load_static(mel, labels)
+        ev = self._phase_begin()
         self._gA.replay()
+        self._phase_mark(ev, "fwd_bwd")
         self._dp_reduce()
+        self._phase_mark(ev, "all_reduce")
         self.flush()
         self._gB.replay()
+        self._phase_mark(ev, "update")
         self._post(self._sbad)
         return self._sloss.clone()
+
+    def _phase_begin(self):
+        if self.phase_events is None:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        rec = {"_last": e}
+        self.phase_events.append(rec)
+        return rec
+
+    @staticmethod
+    def _phase_mark(rec, name):
+        if rec is None:
+            return
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        rec[name] = (rec["_last"], e)
+        rec["_last"] = e
 
     def _load_static(self, mel, labels):
         smel, slab = self._static
@@ -558,9 +711,12 @@ class TrainStep:
                 self.opt.step()
             self._gA, self._gB = gA, gB
         self._load_static(mel, labels)
+        ev = self._phase_begin()
         self._gA.replay()
+        self._phase_mark(ev, "fwd_bwd")
         self.flush()
         self._gB.replay()
+        self._phase_mark(ev, "update")
         self._post(self._sbad)
         return self._sloss.clone()
 
