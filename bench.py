@@ -533,6 +533,49 @@ def step_phase_times(torch, step, batches, world, n=5):
     return {k: round(float(x), 3) for k, x in zip(names, v.tolist())}
 
 
+def write_dp_profile(torch, step, batches, path, rank, n=2):
+    """n replayed data-parallel steps, the kernels of rank 0 under
+    torch.profiler (every rank runs the same steps, so the collectives
+    match): step span, device time of the compute kernels (their union) and
+    of the NCCL kernels, and the NCCL time that no compute kernel overlaps."""
+    import contextlib
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    ctx = profile(activities=[ProfilerActivity.CUDA]) if rank == 0 else contextlib.nullcontext()
+    with ctx as prof:
+        for i in range(n):
+            step.step(*batches[i % 2])
+        torch.cuda.synchronize()
+    if rank != 0:
+        return
+    ev = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                if e.device_type.name == "CUDA" and "Memcpy" not in e.name and "Memset" not in e.name)
+
+    def union(iv):
+        tot, cur = 0.0, None
+        for a, b in sorted(iv):
+            if cur is None or a > cur[1]:
+                if cur is not None:
+                    tot += cur[1] - cur[0]
+                cur = [a, b]
+            else:
+                cur[1] = max(cur[1], b)
+        return tot + (cur[1] - cur[0] if cur else 0.0)
+
+    nccl = [(a, b) for a, b, nm in ev if "nccl" in nm.lower()]
+    comp = [(a, b) for a, b, nm in ev if "nccl" not in nm.lower()]
+    span = ev[-1][1] - ev[0][0]
+    exposed = sum((b - a) - union([(max(a, c), min(b, d)) for c, d in comp if d > a and c < b]) for a, b in nccl)
+    names = sorted({nm.split("(")[0] for _, _, nm in ev if "nccl" in nm.lower()})
+    lines = [f"# {n} replayed steps on rank 0 (us)",
+             f"span {span:.0f}", f"compute busy (union of kernels) {union(comp):.0f}",
+             f"nccl kernels {len(nccl)}, device time {sum(b - a for a, b in nccl):.0f}",
+             f"nccl time overlapped by no compute kernel {exposed:.0f}",
+             "nccl kernel names: " + ", ".join(names)]
+    with open(path, "w") as f:
+        f.write("\n".join(lines) + "\n")
+
+
 def train_sub_bench(torch, device, world, rank, steps=10, warmup=3, profile_path=""):
     """Whisper-small tau-opus + WTA train step (batch 16 per GPU, bf16 autocast,
     fp32 master weights, AdamW); one NCCL all-reduce of all gradients per step
@@ -565,8 +608,10 @@ def train_sub_bench(torch, device, world, rank, steps=10, warmup=3, profile_path
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     phases = step_phase_times(torch, step, batches, world)
-    if profile_path and rank == 0 and world == 1:
+    if profile_path and world == 1:
         write_step_profile(torch, step, batches[0], profile_path)
+    elif profile_path:
+        write_dp_profile(torch, step, batches, profile_path, rank)
     flops = T.model_flops_per_step(cfg)
     peak = load_peaks()[2]
     out = {"samples_per_s": round(world * cfg.batch / (ms * 1e-3), 2), "ms_per_step": round(ms, 2),
@@ -992,7 +1037,8 @@ def main():
                          "train_kernels, fixed")
     ap.add_argument("--torch-profile", default="",
                     help="with --train-only: profile one more step with torch.profiler and write its top "
-                         "device-time ops and the callers of its copy kernels to this file")
+                         "device-time ops and the callers of its copy kernels to this file (1 GPU), or "
+                         "rank 0's compute / NCCL kernel overlap over two replayed steps (N > 1)")
     args = ap.parse_args()
     if args.profile_batch:
         args.quick = args.no_e2e = args.no_cpu = args.no_train = True
