@@ -53,7 +53,7 @@ def log(*a):
 
 # DRAM bytes per launch (read + write) of the main kernels at the encoder_self
 # workload (B=16), from one ncu capture each; traffic grows with B.
-BWD_MAIN_TRAFFIC = 361.4e6
+BWD_MAIN_TRAFFIC = 225.9e6 + 134.5e6   # dram bytes read + written, one ncu capture of the persistent kernel
 FWD_TRAFFIC = 129.2e6
 # WTA forward (encoder, [24000, 3072]): DRAM reads 147.5 MB + writes 101.6 MB in
 # one capture; the writes still in L2 at kernel end are not counted there
