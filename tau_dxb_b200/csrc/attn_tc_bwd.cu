@@ -72,31 +72,12 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kLog2Clamp = -26.575424759098897f;   // log2(1e-8)
 constexpr int kErrTimeoutTma = 1, kErrTimeoutMma = 2, kErrTimeoutCompute = 4;
-#ifndef TAU_BWD_QSTAGES
-#define TAU_BWD_QSTAGES 3
-#endif
-#ifndef TAU_BWD_KVBUFS
-#define TAU_BWD_KVBUFS 2
-#endif
-constexpr int kQStages = TAU_BWD_QSTAGES;     // Q / dO / row-statistics ring
-constexpr int kKVBufs = TAU_BWD_KVBUFS;       // K / V of consecutive items
-#ifndef TAU_BWD_DSBUFS
-#define TAU_BWD_DSBUFS 1
-#endif
-constexpr int kDSBufs = TAU_BWD_DSBUFS;       // dS^T tiles (2 atoms of 64 queries each)
+constexpr int kQStages = 3;      // Q / dO / row-statistics ring
+constexpr int kKVBufs = 2;       // K / V of consecutive items
+constexpr int kDSBufs = 1;       // dS^T tiles (2 atoms of 64 queries each)
 // registers per thread after setmaxnreg: producer warpgroup (TMA, MMA, row
 // statistics), epilogue warpgroup, elementwise warps
-#ifndef TAU_BWD_REG_PRODUCER
-#define TAU_BWD_REG_PRODUCER 64
-#endif
-#ifndef TAU_BWD_REG_EPILOGUE
-#define TAU_BWD_REG_EPILOGUE 64
-#endif
-#ifndef TAU_BWD_REG_COMPUTE
-#define TAU_BWD_REG_COMPUTE 88
-#endif
-#define TDX_BWD_STR2(x) #x
-#define TDX_BWD_STR(x) TDX_BWD_STR2(x)
+constexpr int kRegProducer = 64, kRegEpilogue = 64, kRegCompute = 88;
 
 struct BwdParams {
   CUtensorMap tq, tk, tv, tdo, tdq;
@@ -268,13 +249,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   // Register split of the 80 x 768 launched: producer warpgroup (warps 0-3)
-  // and epilogue warpgroup 48 per thread, elementwise warps 96
-  // (48*128 + 48*128 + 96*512 = 61440). Each warpgroup's code is reached only
-  // through its own setmaxnreg, so the compiler allocates each to its limit.
-  static_assert(TAU_BWD_REG_PRODUCER * 128 + TAU_BWD_REG_EPILOGUE * 128 + TAU_BWD_REG_COMPUTE * 512 <= 80 * kThreads,
-                "register split");
+  // and epilogue warpgroup 64 per thread, elementwise warps 88
+  // (64*128 + 64*128 + 88*512 = 61440; 48 / 48 / 96 spilled in the producer
+  // and epilogue warps). Each warpgroup's code is reached only through its own
+  // setmaxnreg, so the compiler allocates each to its limit.
+  static_assert(kRegProducer * 128 + kRegEpilogue * 128 + kRegCompute * 512 <= 80 * kThreads, "register split");
   if (warp < 4) {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 " TDX_BWD_STR(TAU_BWD_REG_PRODUCER) ";" ::: "memory");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRegProducer) : "memory");
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
     if (lane == 0) {
@@ -443,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     }
   }
   } else if (warp < 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 " TDX_BWD_STR(TAU_BWD_REG_EPILOGUE) ";" ::: "memory");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRegEpilogue) : "memory");
     // ---------------------------------------------------------------- dQ epilogue
     // One thread per query row; dQ_j's 64 TMEM columns in two halves of 32,
     // each scaled by tau*alpha, staged in one 128B-swizzled box and sent with
@@ -576,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_bwd_tc_kernel(const __grid_c
     }
     if (threadIdx.x == 128) tc::bulk_wait_group0();
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 " TDX_BWD_STR(TAU_BWD_REG_COMPUTE) ";" ::: "memory");
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kRegCompute) : "memory");
     // ---------------------------------------------------------------- elementwise
     // Per score: a2 = log2(e) alpha (s scale - m), y = tau log2 sigma,
     // q = 2^max(y, ylo) (both clamps of the reference in one), P = q / Z,
